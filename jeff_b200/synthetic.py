@@ -1,0 +1,206 @@
+"""Seeded synthetic weights, adapters and passes for the decision hot path (no checkpoint or tokenizer exists offline).
+
+Every tensor is drawn from its own CPU generator, seeded from (spec seed, tensor name), so the same spec gives the
+same bits on any machine with the same torch build; GPU code receives copies of these CPU tensors, so the oracle and
+the kernels read identical inputs.
+
+Weights follow the reference benchmark configuration (random init as transformers initialises Qwen3.5: matrices
+N(0, 0.02), RMSNorm weights 0, A_log = log U(0, 16), dt_bias = 1; transformers Qwen3_5PreTrainedModel._init_weights),
+quantised to int4 ("g128z": group 128 with bf16 scale and zero; "g64": the reference's symmetric int4-g64).
+`norm_noise` > 0 perturbs the norm weights (tests use it so that a kernel that ignores a norm weight fails).
+
+Fused groups (the reference's `Lin`, fast_path.py:301-349): matrices reading the same input, concatenated along the
+output. Each adapter's LoRA update of a group is block diagonal: rank 16 per adapted matrix, ranks stacked
+(R = 16 x adapted matrices; the reference pads R to a power of two with zero rows, which adds zeros)."""
+
+from __future__ import annotations
+
+import zlib
+from dataclasses import dataclass, field
+
+import torch
+
+from jeff_b200 import constants as C
+from jeff_b200.int4 import PackedInt4, quantize_pack
+
+DT = torch.bfloat16
+
+
+def generator(seed: int, name: str) -> torch.Generator:
+    """The CPU generator of one named tensor under a spec seed."""
+    return torch.Generator().manual_seed((seed * 1_000_003 + zlib.crc32(name.encode())) % (2**63))
+
+
+def normal(seed: int, name: str, shape: tuple[int, ...], std: float, mean: float = 0.0) -> torch.Tensor:
+    return torch.randn(*shape, generator=generator(seed, name)) * std + mean
+
+
+def uniform(seed: int, name: str, shape: tuple[int, ...], lo: float, hi: float) -> torch.Tensor:
+    return torch.rand(*shape, generator=generator(seed, name)) * (hi - lo) + lo
+
+
+@dataclass
+class FusedGroup:
+    """Matrices that read the same input, concatenated along the output (module docstring)."""
+    names: list[str]
+    sizes: list[int]
+    k: int
+    packed: PackedInt4
+    W: torch.Tensor            # (out, k) bf16: the dequantised weights, as the standard path multiplies by them
+    adapted: list[bool]        # which matrices an adapter adapts
+    rank: int                  # R = 16 x adapted matrices (0: no LoRA on this group)
+
+    @property
+    def out(self) -> int:
+        return sum(self.sizes)
+
+
+@dataclass
+class LayerWeights:
+    kind: str
+    norm_in: torch.Tensor      # (1024,) float32: the RMSNorm weight w (the kernels scale by 1 + w)
+    norm_post: torch.Tensor
+    groups: dict[str, FusedGroup]
+    conv: torch.Tensor | None = None      # (6144, 4) bf16 depthwise weights
+    A_log: torch.Tensor | None = None     # (16,) float32
+    dt_bias: torch.Tensor | None = None   # (16,) float32
+    gnorm: torch.Tensor | None = None     # (128,) bf16, plain weight (no 1 +)
+    q_norm: torch.Tensor | None = None    # (256,) float32 w (1 + w applied)
+    k_norm: torch.Tensor | None = None
+
+
+@dataclass
+class ModelSpec:
+    layers: int = C.LAYERS
+    vocab: int = C.VOCAB
+    fmt: str = "g128z"
+    seed: int = 4
+    norm_noise: float = 0.0
+
+
+@dataclass
+class ModelWeights:
+    spec: ModelSpec
+    kinds: list[str]
+    embed: torch.Tensor        # (vocab, 1024) bf16
+    final_norm: torch.Tensor   # (1024,) float32 w
+    layers: list[LayerWeights] = field(default_factory=list)
+
+
+def _group(seed: int, prefix: str, names: list[str], sizes: list[int], k: int, fmt: str) -> FusedGroup:
+    ws = [normal(seed, prefix + n, (s, k), 0.02) for n, s in zip(names, sizes, strict=True)]
+    packed, deq = quantize_pack(torch.cat(ws), fmt)
+    adapted = [n.rsplit(".", 1)[-1] in C.LORA_TARGETS for n in names]
+    return FusedGroup([prefix + n for n in names], sizes, k, packed, deq, adapted, C.LORA_RANK * sum(adapted))
+
+
+def make_model(spec: ModelSpec) -> ModelWeights:
+    """The synthetic base of `spec` (module docstring). The layer kinds repeat (GDN, GDN, GDN, attention)."""
+    s = spec.seed
+    kinds = [C.LAYER_KINDS[i % 4] for i in range(spec.layers)]
+    embed = normal(s, "embed_tokens", (spec.vocab, C.HIDDEN), 0.02).to(DT)
+
+    def norm(name: str, n: int) -> torch.Tensor:
+        if spec.norm_noise:
+            return normal(s, name, (n,), spec.norm_noise)
+        return torch.zeros(n)
+
+    model = ModelWeights(spec, kinds, embed, norm("norm", C.HIDDEN))
+    for i, kind in enumerate(kinds):
+        p = f"layers.{i}."
+        groups = {
+            "mlp_in": _group(s, p, ["mlp.gate_proj", "mlp.up_proj"], [C.INTER, C.INTER], C.HIDDEN, spec.fmt),
+            "mlp_down": _group(s, p, ["mlp.down_proj"], [C.HIDDEN], C.INTER, spec.fmt),
+        }
+        layer = LayerWeights(kind, norm(p + "input_layernorm", C.HIDDEN), norm(p + "post_attention_layernorm", C.HIDDEN),
+                             groups)
+        if kind == "linear_attention":
+            la = "linear_attn."
+            groups["proj"] = _group(s, p, [la + "in_proj_qkv", la + "in_proj_z", la + "in_proj_b", la + "in_proj_a"],
+                                    [C.QKV_DIM, C.Z_DIM, C.NV, C.NV], C.HIDDEN, spec.fmt)
+            groups["out"] = _group(s, p, [la + "out_proj"], [C.HIDDEN], C.NV * C.DV, spec.fmt)
+            layer.conv = uniform(s, p + la + "conv1d", (C.QKV_DIM, C.CONV), -0.5, 0.5).to(DT)
+            layer.A_log = torch.log(uniform(s, p + la + "A_log", (C.NV,), 0.0, 16.0).clamp_min(1e-3))
+            layer.dt_bias = torch.ones(C.NV) + (normal(s, p + la + "dt_bias", (C.NV,), spec.norm_noise)
+                                                if spec.norm_noise else 0.0)
+            g = torch.ones(C.DV) + (normal(s, p + la + "norm", (C.DV,), spec.norm_noise) if spec.norm_noise else 0.0)
+            layer.gnorm = g.to(DT)
+        else:
+            sa = "self_attn."
+            groups["proj"] = _group(s, p, [sa + "q_proj", sa + "k_proj", sa + "v_proj"],
+                                    [C.NQ * 2 * C.HD, C.NKV * C.HD, C.NKV * C.HD], C.HIDDEN, spec.fmt)
+            groups["out"] = _group(s, p, [sa + "o_proj"], [C.HIDDEN], C.NQ * C.HD, spec.fmt)
+            layer.q_norm = norm(p + sa + "q_norm", C.HD)
+            layer.k_norm = norm(p + sa + "k_norm", C.HD)
+        model.layers.append(layer)
+    return model
+
+
+@dataclass
+class AdapterWeights:
+    """One adapter: per fused group (layer, group key) the stacked A (R, k) and block-diagonal B (out, R), both bf16
+    with the scale alpha / r folded into B (the reference LoraLinear's "model" precision, lora.py:204-210); its
+    readout (255, 1024) bf16 and temperature."""
+    name: str
+    lora: dict[tuple[int, str], tuple[torch.Tensor, torch.Tensor]]
+    readout: torch.Tensor
+    temperature: float
+    matrices: dict[str, tuple[torch.Tensor, torch.Tensor]] = field(default_factory=dict)  # per matrix (A, sB)
+
+
+def make_adapter(model: ModelWeights, index: int, seed: int, alpha: float = 32.0) -> AdapterWeights:
+    """A rank-16 adapter of every LoRA target: A ~ N(0, 0.02), B ~ N(0, 0.01), scale alpha / 16; readout
+    N(0, 0.02); temperature U(0.5, 2)."""
+    name = f"adapter-{index}"
+    scale = alpha / C.LORA_RANK
+    lora: dict[tuple[int, str], tuple[torch.Tensor, torch.Tensor]] = {}
+    matrices: dict[str, tuple[torch.Tensor, torch.Tensor]] = {}
+    for i, layer in enumerate(model.layers):
+        for key, grp in layer.groups.items():
+            if not grp.rank:
+                continue
+            a_all = torch.zeros(grp.rank, grp.k, dtype=DT)
+            b_all = torch.zeros(grp.out, grp.rank, dtype=DT)
+            r0 = o0 = 0
+            for mname, size, adapted in zip(grp.names, grp.sizes, grp.adapted, strict=True):
+                if adapted:
+                    a = normal(seed, f"{name}/{mname}/A", (C.LORA_RANK, grp.k), 0.02).to(DT)
+                    b = (normal(seed, f"{name}/{mname}/B", (size, C.LORA_RANK), 0.01) * scale).to(DT)
+                    a_all[r0:r0 + C.LORA_RANK] = a
+                    b_all[o0:o0 + size, r0:r0 + C.LORA_RANK] = b
+                    matrices[mname] = (a, b)
+                    r0 += C.LORA_RANK
+                o0 += size
+            lora[(i, key)] = (a_all, b_all)
+    readout = normal(seed, f"{name}/readout", (C.READOUT_ROWS, C.HIDDEN), 0.02).to(DT)
+    temperature = float(uniform(seed, f"{name}/temperature", (1,), 0.5, 2.0)[0])
+    return AdapterWeights(name, lora, readout, temperature, matrices)
+
+
+def base_head(model: ModelWeights) -> tuple[torch.Tensor, float]:
+    """The base's own readout (adapter row 0) and temperature."""
+    return normal(model.spec.seed, "readout", (C.READOUT_ROWS, C.HIDDEN), 0.02).to(DT), 1.0
+
+
+@dataclass
+class PassRows:
+    """One decision pass's rows: adapter index (0 the base, i the i-th adapter), prefix token ids, new token ids,
+    option count."""
+    adapters: list[int]
+    prefixes: list[list[int]]
+    new_ids: list[list[int]]
+    counts: list[int]
+
+
+def make_cfg4_rows(seed: int, calls: int = 64, new_tokens: int = 128, prefix_tokens: int = 512, adapters: int = 16,
+                   vocab: int = C.VOCAB) -> PassRows:
+    """The reference benchmark configuration 4: `calls` calls of `new_tokens` tokens, each on its adapter's shared
+    `prefix_tokens`-token prefix (one prefix per adapter), adapters uniform over 1..adapters, option counts
+    U{2..32}, token ids uniform over the vocabulary."""
+    g = generator(seed, "cfg4/rows")
+    prefix_of = {a: torch.randint(0, vocab, (prefix_tokens,), generator=generator(seed, f"cfg4/prefix/{a}")).tolist()
+                 for a in range(1, adapters + 1)}
+    chosen = torch.randint(1, adapters + 1, (calls,), generator=g).tolist()
+    new = torch.randint(0, vocab, (calls, new_tokens), generator=g).tolist()
+    counts = torch.randint(2, 33, (calls,), generator=g).tolist()
+    return PassRows(chosen, [prefix_of[a] for a in chosen], new, counts)
