@@ -1,0 +1,145 @@
+/* libjeffb200: the C ABI of the B200-native decision hot path (sm_100a).
+ *
+ * Every entry point takes raw device pointers, sizes and a cudaStream_t (as void*), launches its kernels on that
+ * stream and returns a status (JB_OK or a negative code; jb_last_error() gives the message). No entry point
+ * allocates device memory or synchronises, so all of them can be recorded into a CUDA graph; buffers belong to the
+ * caller. bf16 tensors are passed as uint16_t* (bfloat16 bit patterns), row-major and contiguous unless a leading
+ * dimension is given.
+ *
+ * Each declaration names the reference interface it replaces (firelex/jeff, paths under
+ * runtime/python/src/jeff_runtime/engine/). The prefix pool geometry is the reference's (prefix_pool.py:1-40):
+ * pages of page_bytes bytes; state[page][head slot][128][128] fp32, conv[page][layer slot][3][6144] bf16,
+ * kv[page][attn layer][K|V][32 tokens][2 heads][256] bf16; block tables int32 [row][state pages | conv pages |
+ * key/value pages]. */
+#ifndef JEFFB200_H
+#define JEFFB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define JB_OK 0
+#define JB_EINVAL (-1)   /* an argument the kernels cannot take (checked before any launch) */
+#define JB_ECUDA (-2)    /* a CUDA runtime error */
+#define JB_ETIMEOUT (-3) /* a device-side bounded wait gave up (see jb_device_status) */
+#define JB_DEV_TIMEOUT 0x10000 /* device status word: a bounded wait gave up; low bits say where */
+
+/* ABI version of this header (bumped on any signature change). */
+int jb_abi_version(void);
+/* The message of the last failure on the calling thread ("" if none). */
+const char* jb_last_error(void);
+/* Reads (and with reset != 0 clears) this device's status word that kernels set when a bounded wait gives up.
+ * Synchronises `stream`. Not for use inside graph capture. */
+int jb_device_status(int* status, int reset, void* stream);
+
+/* ---------------------------------------------------------------- int4 W4A16 + multi-LoRA products (S1) */
+
+/* Dequantise a packed group (for verification): words int32 (k/8, columns), scales and zeros (nullable) bf16
+ * (k/group, columns) -> out bf16 (columns, k), bf16(fp32(u - z) * fp32(s)) with z = 8 when zeros is NULL.
+ * Replaces int4.dequantize / unpack_kernel (int4.py:203-208, :258-262). */
+int jb_int4_dequant(const int32_t* words, const uint16_t* scales, const uint16_t* zeros, int k, int columns,
+                    int group, uint16_t* out, void* stream);
+
+/* LoRA first factor: mid (m, rank) bf16 = bf16(x (m, k) . A[a]^T) with fp32 accumulation in input order, A from
+ * lora_a (pool_rows, rank, k) in the row a = adapters[t / row_len] of token t. Replaces fast_path._lora_mid_kernel
+ * (fast_path.py:159-177) and int4_kernels._lora_mid_tile (int4_kernels.py:65-82). */
+int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* lora_a, int rank, int pool_rows,
+                   const int32_t* adapters, int row_len, uint16_t* mid, void* stream);
+
+/* The fused product: y (m, out) bf16 = bf16(x . W^T + mid . B[a]^T), W = dequantised int4 (words, scales, zeros as
+ * jb_int4_dequant), the base product accumulated in fp32 by tcgen05 tensor cores from TMA-staged packed weights
+ * dequantised in shared memory, then the LoRA expand (mid from jb_lora_shrink, B from lora_b (pool_rows, columns,
+ * rank)) added into the same accumulator, rounded once. rank 0 (or mid NULL) leaves out the LoRA term.
+ * Requires k % 64 == 0, columns % 64 == 0, out <= columns, ldy % 8 == 0, row_len % 32 == 0 and row_len % 128 == 0
+ * or 128 % row_len == 0. Replaces int4_kernels.int4_product (int4_kernels.py:132-177) and Lin.__call__
+ * (fast_path.py:347-349). */
+int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
+                  const uint16_t* zeros, int group, int columns, int out, const uint16_t* mid, const uint16_t* lora_b,
+                  int rank, int pool_rows, const int32_t* adapters, int row_len, uint16_t* y, int ldy, void* stream);
+
+/* jb_lora_shrink then jb_w4a16_lora, with the caller's scratch `mid` (at least m * rank bf16). */
+int jb_int4_lora_product(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
+                         const uint16_t* zeros, int group, int columns, int out, const uint16_t* lora_a,
+                         const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
+                         uint16_t* mid, uint16_t* y, int ldy, void* stream);
+
+/* ---------------------------------------------------------------- fused norms and activations (S4) */
+
+/* xo = bf16(x + d) (d NULL: xo = x, may alias), h = bf16(rms(xo) * w1), w1 = 1 + weight (fp32, n). rows x n.
+ * Replaces fast_path.add_rms (fast_path.py:80-100). */
+int jb_add_rms(const uint16_t* x, const uint16_t* d, const float* w1, uint16_t* xo, uint16_t* h, int rows, int n,
+               void* stream);
+/* hidden (b, n) = bf16(rms(bf16(x[t] + d[t])) * w1) at each row's last real token t = r * row_len + last[r].
+ * Replaces the final norm of batched_path.body (batched_path.py:274-275). */
+int jb_rms_last(const uint16_t* x, const uint16_t* d, const int32_t* last, int b, int row_len, int n,
+                const float* w1, uint16_t* hidden, void* stream);
+/* x (t, dim) = table[ids] (embedding gather). Replaces embed.index_select (batched_path.py:251). */
+int jb_embed(const uint16_t* table, int vocab, int dim, const int32_t* ids, int t, uint16_t* x, void* stream);
+/* y (rows, inter) = bf16(bf16(silu(g)) * u), g = gu[:, :inter], u = gu[:, inter:2 inter].
+ * Replaces fast_path.silu_mul (fast_path.py:141-156). */
+int jb_silu_mul(const uint16_t* gu, int ldgu, int inter, uint16_t* y, int rows, void* stream);
+/* y (rows, 2048) = bf16(o * bf16(sigmoid(gate))), o (rows, 8, 256), gate from pr's query/gate interleave.
+ * Replaces fast_path.gate_mul (fast_path.py:123-138). */
+int jb_gate_mul(const uint16_t* o, const uint16_t* pr, int ldpr, uint16_t* y, int rows, void* stream);
+/* Gated DeltaNet output norm: y (rows, 2048) = bf16(bf16(w * bf16(rms(o))) * silu(z)), per head of 128,
+ * z = pr[:, z_off:z_off + 2048]. Replaces fast_path.gated_norm (fast_path.py:103-120). */
+int jb_gated_norm(const uint16_t* o, const uint16_t* pr, int ldpr, int z_off, const uint16_t* w, uint16_t* y,
+                  int rows, void* stream);
+/* Per-row readout and option softmax: probs (b, 255) fp32 from hidden (b, 1024) and the row's adapter readout
+ * (pool_rows, 255, 1024) bf16: logits bf16(W h) (fp32 sums), options >= counts[r] to -1e9, / temp_pool[a], softmax.
+ * Replaces batched_kernels.readout_rows (batched_kernels.py:492-559). */
+int jb_readout_rows(const uint16_t* hidden, const uint16_t* readout_pool, int pool_rows, const float* temp_pool,
+                    const int32_t* adapters, const int32_t* counts, int b, float* probs, void* stream);
+
+/* ---------------------------------------------------------------- Gated DeltaNet (S2) */
+
+/* Input side for t = b * n tokens (rows of n): causal width-4 conv over the row's 3 cached inputs (its conv page
+ * tables[r][conv_entry], layer slot conv_slot) and its new ones, SiLU -> bf16, q/k L2-normalised -> bf16, v;
+ * g = a_neg * softplus(a + dt_bias) fp32, beta = bf16(sigmoid(b)). pr (t, ldpr >= 8224) = [qkv | z | b | a].
+ * real (nullable, the prefix pass): tokens from real[r] on get g = 0, beta = 0, and the row's last three real conv
+ * inputs are written to its output conv page out_tables[r][conv_entry] (zeros first when real < 3).
+ * Replaces batched_kernels.gdn_prep_rows (batched_kernels.py:89-194). */
+int jb_gdn_prep_rows(const uint16_t* pr, int ldpr, int t, int n, void* pool, int64_t page_bytes,
+                     const int32_t* tables, int table_stride, int conv_entry, int conv_slot, const float* conv_w,
+                     const float* a_neg, const float* dt_bias, uint16_t* q, uint16_t* k, uint16_t* v, float* g,
+                     uint16_t* beta, const int32_t* real, const int32_t* out_tables, int out_table_stride,
+                     void* stream);
+/* The gated delta rule over each row's n tokens from its state read in place from the pool (flat head
+ * first_head + h at tables[r][(first_head + h) / heads_per_page], slot % heads_per_page); o (b, n, 16, 128) bf16.
+ * last (nullable): stop after last[r] and write zeros past it. out_tables (nullable, the prefix pass): write each
+ * row's final state into its own state pages. Replaces batched_kernels.gdn_recurrent_slots (:200-261) and fla's
+ * chunk_gated_delta_rule at batched_path.py:282-288, :322-324. */
+int jb_gdn_scan(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g, const uint16_t* beta,
+                uint16_t* o, int b, int n, void* pool, int64_t page_bytes, const int32_t* tables, int table_stride,
+                int first_head, int heads_per_page, const int32_t* last, const int32_t* out_tables,
+                int out_table_stride, void* stream);
+
+/* ---------------------------------------------------------------- attention (S3) */
+
+/* Attention input side: per token q/k per-head RMSNorm * w1 -> bf16, RoPE on the first 64 dims at position
+ * pos[r] + j (inv_freq (32,) fp32; cos and sin rounded to bf16); q (t, 8, 256), kn, vn (t, 2, 256).
+ * Replaces batched_kernels.attn_prep_rows (batched_kernels.py:302-364). */
+int jb_attn_prep_rows(const uint16_t* pr, int ldpr, int t, int n, const float* q_w1, const float* k_w1,
+                      const float* inv_freq, const int32_t* pos, uint16_t* q, uint16_t* kn, uint16_t* vn,
+                      void* stream);
+/* Each row's queries over its prefix (pos[r] tokens in the key/value pages tables[r][kv_entry + j / 32]) fully,
+ * then its own new keys causally; GQA 8 query / 2 key-value heads of 256, softmax scale 1/16, weights rounded to
+ * bf16 before the value product; out (t, 8, 256) bf16. Replaces batched_kernels.paged_attention
+ * (batched_kernels.py:370-486) and the prefix pass's scaled_dot_product_attention (batched_path.py:333-336). */
+int jb_paged_attention(const uint16_t* q, const void* pool, int64_t page_bytes, const int32_t* tables,
+                       int table_stride, int kv_entry, int attn_layer, int attn_layers, const int32_t* pos,
+                       const uint16_t* kn, const uint16_t* vn, uint16_t* out, int b, int n, void* stream);
+/* The prefix pass's page scatter: each row's new keys/values (tokens below ceil(real[r] / 32) * 32) into its
+ * pages out_tables[r][kv_entry + j / 32] of attention layer attn_layer. Replaces pool.kv.index_copy_
+ * (batched_path.py:345-349). */
+int jb_kv_scatter(const uint16_t* kn, const uint16_t* vn, int b, int n, const int32_t* real, void* pool,
+                  int64_t page_bytes, const int32_t* out_tables, int table_stride, int kv_entry, int attn_layer,
+                  int attn_layers, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* JEFFB200_H */

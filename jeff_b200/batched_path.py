@@ -1,0 +1,447 @@
+"""The batched decision path on B200 (the reference's engine/batched_path.py BatchedPath, :177-752): one CUDA graph
+replay answers up to 64 rows, each with its own adapter and cached prefix, on a FastPath's weights and pools.
+
+A pass holds B rows of N new tokens (T = B * N, row after row), each row padded to N after its last real token;
+every layer is causal, so padding never reaches a real token. One graph per (B, N), recorded on first use (or all
+at start with record()); everything a graph reads per row comes from ONE packed int32 input buffer in device memory
+(batched_path.py:45-50): [slot, adapter, prefix length, last, count] x B, then the B x N token ids, filled on the
+host with numpy into a pinned twin and copied in with one copy; the probabilities (B x 255) come back in one copy.
+All intermediate tensors live in one preallocated Workspace, so capture and replay allocate nothing.
+
+Batched prefix passes (batched_path.py:291-349, :613-744): new prefixes are processed B at a time from the empty
+state, each row writing its final Gated DeltaNet states, convolution tails and attention keys/values straight into its
+own slot's pages (the kernels take the rows' page lists from the prefix input buffer).
+
+Calls are serialised by the caller (the engine's GPU thread), adapter changes between passes."""
+
+from __future__ import annotations
+
+import time
+from collections.abc import Callable, Sequence
+from dataclasses import dataclass
+from typing import Any
+
+import numpy as np
+import torch
+
+from jeff_b200 import constants as C
+from jeff_b200 import kernels
+from jeff_b200.fast_path import FastPath
+from jeff_b200.prefix_pool import PAGE_TOKENS, SINK_PAGE, ZERO_PAGE
+
+DT = torch.bfloat16
+PASS_SHAPES = tuple((b, n) for n in C.NEW_BUCKETS for b in C.BATCH_BUCKETS if b * n <= C.MAX_PASS_TOKENS)
+PREFIX_PASS_ROWS = {64: 16, 128: 32, 256: 16, 512: 8, 768: 4, 1024: 4, 1536: 4, 2048: 2, 3072: 2, 4096: 1,
+                    6144: 1, 8192: 1}
+PREFIX_META = 2
+
+
+@dataclass
+class Row:
+    """One question ready for the fast path (the reference's prepare.Row): prefix text, new token ids, options."""
+    prefix_text: str
+    new_ids: list[int]
+    count: int
+
+
+def max_rows(n: int) -> int:
+    return max(b for b in C.BATCH_BUCKETS if b * n <= C.MAX_PASS_TOKENS)
+
+
+class Workspace:
+    """Every intermediate tensor of a pass of up to `tokens` tokens and `rows` rows."""
+
+    def __init__(self, tokens: int, rows: int, width: int, max_rank: int, device: torch.device) -> None:
+        def e(*shape: int, dtype: torch.dtype = DT) -> torch.Tensor:
+            return torch.empty(*shape, dtype=dtype, device=device)
+
+        self.tokens, self.rows = tokens, rows
+        self.x = e(tokens, C.HIDDEN)
+        self.h = e(tokens, C.HIDDEN)
+        self.d = e(tokens, C.HIDDEN)
+        self.pr = e(tokens * C.GDN_PROJ)
+        self.q = e(tokens * C.NV * C.DK)
+        self.k = e(tokens * C.NV * C.DK)
+        self.v = e(tokens * C.NV * C.DV)
+        self.g = e(tokens * C.NV, dtype=torch.float32)
+        self.beta = e(tokens * C.NV)
+        self.o = e(tokens * C.NV * C.DV)
+        self.y = e(tokens, C.NQ * C.HD)
+        self.aq = e(tokens, C.NQ, C.HD)
+        self.ao = e(tokens, C.NQ, C.HD)
+        self.kn = e(tokens, C.NKV, C.HD)
+        self.vn = e(tokens, C.NKV, C.HD)
+        self.gu = e(tokens, 2 * C.INTER)
+        self.act = e(tokens, C.INTER)
+        self.mid = e(tokens * max(max_rank, 16))
+        self.tables = torch.zeros(rows, width, dtype=torch.int32, device=device)
+        self.zero_tables = torch.zeros(rows, width, dtype=torch.int32, device=device)
+        self.zero_pos = torch.zeros(rows, dtype=torch.int32, device=device)
+        self.hidden = e(rows, C.HIDDEN)
+        self.probs = e(rows, C.READOUT_ROWS, dtype=torch.float32)
+
+
+class BatchedPath:
+    def __init__(self, fast: FastPath, tokenize: Callable[[str], list[int]] | None = None,
+                 max_tokens: int = C.MAX_PASS_TOKENS, max_rows_per_pass: int = max(C.BATCH_BUCKETS)) -> None:
+        self.fast = fast
+        self.pool = fast.prefixes
+        self.tokenize = tokenize
+        self.max_tokens = max_tokens
+        dev = fast.device
+        self.device = dev
+        width = self.pool.width
+        self.ws = Workspace(max_tokens, max_rows_per_pass, width, fast.max_rank, dev)
+        self.ws.zero_tables[:, :self.pool.fixed_pages] = ZERO_PAGE
+        size = max(C.META * b + b * n for b, n in PASS_SHAPES)
+        self.inp = torch.zeros(size, dtype=torch.int32, device=dev)
+        self.inp_host = torch.zeros(size, dtype=torch.int32).pin_memory()
+        self.inp_np = self.inp_host.numpy()
+        self.out_host = torch.zeros(max(C.BATCH_BUCKETS), C.READOUT_ROWS, dtype=torch.float32).pin_memory()
+        psize = max((PREFIX_META + self._prefix_width(nb) + nb) * b for nb, cap in PREFIX_PASS_ROWS.items()
+                    for b in C.BATCH_BUCKETS if b <= cap and b * nb <= max_tokens) if max_tokens >= 64 else 1
+        self.prefix_inp = torch.zeros(psize, dtype=torch.int32, device=dev)
+        self.prefix_inp_host = torch.zeros(psize, dtype=torch.int32).pin_memory()
+        self.prefix_inp_np = self.prefix_inp_host.numpy()
+        self.graphs: dict[tuple[int, int], tuple[torch.cuda.CUDAGraph, torch.Tensor]] = {}
+        self.prefix_graphs: dict[tuple[int, int], torch.cuda.CUDAGraph] = {}
+        self.graph_pool = torch.cuda.graph_pool_handle()
+        self.stream = torch.cuda.Stream(device=dev)
+        self.start = torch.cuda.Event(enable_timing=True)
+        self.end = torch.cuda.Event(enable_timing=True)
+
+    # ------------------------------------------------------------ input views
+
+    def views(self, b: int, n: int) -> dict[str, torch.Tensor]:
+        meta = self.inp[:C.META * b].view(C.META, b)
+        return {"slots": meta[0], "adapters": meta[1], "pos": meta[2], "last": meta[3], "counts": meta[4],
+                "ids": self.inp[C.META * b:C.META * b + b * n]}
+
+    def _prefix_width(self, nb: int) -> int:
+        return self.pool.fixed_pages + nb // PAGE_TOKENS
+
+    def prefix_views(self, b: int, nb: int) -> dict[str, torch.Tensor]:
+        w = self._prefix_width(nb)
+        meta = self.prefix_inp[:PREFIX_META * b].view(PREFIX_META, b)
+        pages = self.prefix_inp[PREFIX_META * b:(PREFIX_META + w) * b].view(b, w)
+        ids = self.prefix_inp[(PREFIX_META + w) * b:(PREFIX_META + w + nb) * b]
+        return {"adapters": meta[0], "lengths": meta[1], "pages": pages, "ids": ids}
+
+    # ------------------------------------------------------------ the passes
+
+    def _layers(self, x: torch.Tensor, adapters: torch.Tensor, n: int, t: int, gdn_tables: torch.Tensor,
+                attn_tables: torch.Tensor, pos: torch.Tensor, last: torch.Tensor | None,
+                real: torch.Tensor | None = None, out_tables: torch.Tensor | None = None) -> torch.Tensor | None:
+        """The decoder layers over t tokens (rows of n), in place on the residual x; returns the last d."""
+        f, ws, pool = self.fast, self.ws, self.pool
+        b = t // n
+        d: torch.Tensor | None = None
+        gi = ai = 0
+        prefix = out_tables is not None
+        for li, layer in enumerate(f.layers):
+            _, h = kernels.add_rms(x, d, layer["norm_in"], xo=x, h=ws.h[:t])
+            proj = layer["proj"]
+            pr = proj(h, adapters, n, ws.mid, ws.pr[:t * proj.out].view(t, proj.out))
+            if layer["kind"] == "linear_attention":
+                size = t * C.NV * C.DK
+                outs = (ws.q[:size].view(b, n, C.NV, C.DK), ws.k[:size].view(b, n, C.NV, C.DK),
+                        ws.v[:size].view(b, n, C.NV, C.DV), ws.g[:t * C.NV].view(b, n, C.NV),
+                        ws.beta[:t * C.NV].view(b, n, C.NV))
+                q, k, v, g, beta = kernels.gdn_prep_rows(pr, pool, gdn_tables, gi, layer["conv"], layer["a_neg"],
+                                                         layer["dt_bias"], n, real=real, out_tables=out_tables,
+                                                         outs=outs)
+                o = kernels.gdn_scan(q, k, v, g, beta, pool, gdn_tables, gi, last=last, out_tables=out_tables,
+                                     out=ws.o[:size].view(b, n, C.NV, C.DV))
+                y = kernels.gated_norm(o, pr, layer["gnorm"], out=ws.y[:t, :C.NV * C.DV])
+                gi += 1
+            else:
+                kn, vn = ws.kn[:t], ws.vn[:t]
+                aq = kernels.attn_prep_rows(pr, layer["q_w1"], layer["k_w1"], f.inv_freq, pos, kn, vn, n,
+                                            out=ws.aq[:t])
+                if prefix:
+                    assert real is not None and out_tables is not None
+                    kernels.kv_scatter(kn, vn, n, real, pool, out_tables, ai)
+                    if li == len(f.layers) - 1:
+                        return None   # the last layer: only its keys and values are kept
+                ao = kernels.paged_attention(aq, pool, attn_tables, ai, pos, kn, vn, n, out=ws.ao[:t])
+                y = kernels.gate_mul(ao, pr, out=ws.y[:t])
+                ai += 1
+            d = layer["out"](y, adapters, n, ws.mid, ws.d[:t])
+            _, h = kernels.add_rms(x, d, layer["norm_post"], xo=x, h=ws.h[:t])
+            gu = layer["mlp_in"](h, adapters, n, ws.mid, ws.gu[:t])
+            act = kernels.silu_mul(gu, out=ws.act[:t])
+            d = layer["mlp_down"](act, adapters, n, ws.mid, ws.d[:t])
+        return d
+
+    def body(self, b: int, n: int) -> torch.Tensor:
+        """The recorded decision pass: B rows of N tokens from the packed input; returns probabilities (B, 255)."""
+        f, ws = self.fast, self.ws
+        v = self.views(b, n)
+        t = b * n
+        tables = ws.tables[:b]
+        torch.index_select(self.pool.tables, 0, v["slots"], out=tables)
+        x = kernels.embed(f.embed, v["ids"], out=ws.x[:t])
+        d = self._layers(x, v["adapters"], n, t, tables, tables, v["pos"], v["last"])
+        assert d is not None
+        hidden = kernels.rms_last(x, d, v["last"], n, f.final_w1, out=ws.hidden[:b])
+        return kernels.readout_rows(hidden, f.readout_pool, f.temp_pool, v["adapters"], v["counts"],
+                                    out=ws.probs[:b])
+
+    def prefix_body(self, b: int, nb: int) -> None:
+        """The recorded prefix pass: B prefixes of at most nb tokens from the empty state, each row's state written
+        into the pages its row of the prefix input lists (padding rows list the sink page only)."""
+        f, ws = self.fast, self.ws
+        if f.kinds[-1] != "full_attention":
+            raise ValueError("The batched prefix pass expects the last layer to be an attention layer")
+        v = self.prefix_views(b, nb)
+        t = b * nb
+        x = kernels.embed(f.embed, v["ids"], out=ws.x[:t])
+        self._layers(x, v["adapters"], nb, t, ws.zero_tables[:b], ws.zero_tables[:b], ws.zero_pos[:b], None,
+                     real=v["lengths"], out_tables=v["pages"])
+
+    # ------------------------------------------------------------ graphs
+
+    def _capture(self, work: Callable[[], Any]) -> tuple[torch.cuda.CUDAGraph, Any]:
+        self.stream.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(self.stream):
+            for _ in range(2):
+                work()
+        self.stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, pool=self.graph_pool, stream=self.stream):
+            out = work()
+        torch.cuda.current_stream(self.device).wait_stream(self.stream)
+        return graph, out
+
+    def _pad_decision(self, b: int, n: int) -> None:
+        meta = self.inp_np[:C.META * b].reshape(C.META, b)
+        meta[:4] = 0
+        meta[3] = n - 1
+        meta[4] = 2
+        self.inp_np[C.META * b:C.META * b + b * n] = 0
+        self.inp[:C.META * b + b * n].copy_(self.inp_host[:C.META * b + b * n])
+
+    def graph(self, b: int, n: int) -> tuple[torch.cuda.CUDAGraph, torch.Tensor]:
+        if (b, n) not in self.graphs:
+            if b * n > self.max_tokens:
+                raise ValueError(f"A pass of {b} x {n} tokens exceeds this path's workspace ({self.max_tokens})")
+            self._pad_decision(b, n)
+            self.graphs[(b, n)] = self._capture(lambda: self.body(b, n))
+        return self.graphs[(b, n)]
+
+    def _pad_prefix(self, b: int, nb: int) -> None:
+        w = self._prefix_width(nb)
+        size = (PREFIX_META + w + nb) * b
+        self.prefix_inp_np[:size] = 0
+        self.prefix_inp_np[b:2 * b] = nb // 2
+        self.prefix_inp_np[PREFIX_META * b:(PREFIX_META + w) * b] = SINK_PAGE
+        self.prefix_inp[:size].copy_(self.prefix_inp_host[:size])
+
+    def prefix_graph(self, b: int, nb: int) -> torch.cuda.CUDAGraph:
+        if (b, nb) not in self.prefix_graphs:
+            if b * nb > self.max_tokens:
+                raise ValueError(f"A prefix pass of {b} x {nb} tokens exceeds this path's workspace")
+            self._pad_prefix(b, nb)
+            self.prefix_graphs[(b, nb)] = self._capture(lambda: self.prefix_body(b, nb))[0]
+        return self.prefix_graphs[(b, nb)]
+
+    def record(self, shapes: Sequence[tuple[int, int]] | None = None) -> float:
+        """Record the decision graphs of `shapes` (every PASS_SHAPES shape the workspace holds by default)."""
+        started = time.perf_counter()
+        for b, n in shapes if shapes is not None else [s for s in PASS_SHAPES if s[0] * s[1] <= self.max_tokens]:
+            self.graph(b, n)
+        torch.cuda.synchronize(self.device)
+        return time.perf_counter() - started
+
+    # ------------------------------------------------------------ requests
+
+    def fill(self, b: int, n: int, part: Sequence[tuple[int, int, Row]], lengths: Sequence[int]) -> int:
+        """Stage rows into the pinned input buffer (padding rows: slot 0, adapter 0, one token, one option)."""
+        size = C.META * b + b * n
+        meta = self.inp_np[:C.META * b].reshape(C.META, b)
+        ids = self.inp_np[C.META * b:size]
+        meta[:4] = 0
+        meta[4] = 1
+        ids[:] = 0
+        for j, (adapter, slot, row) in enumerate(part):
+            real = len(row.new_ids)
+            if real > n:
+                raise AssertionError(f"{real} new tokens staged in a pass of {n}")
+            ids[j * n:j * n + real] = row.new_ids
+            meta[:, j] = (slot, adapter, lengths[j], real - 1, row.count)
+        return size
+
+    def run_pass(self, b: int, n: int, part: Sequence[tuple[int, int, Row]], lengths: Sequence[int]) -> tuple[
+            np.ndarray, float]:
+        """One pass: H2D of the packed input, graph replay, D2H of the probabilities. Returns (probs (B, 255), ms)."""
+        graph, out = self.graph(b, n)
+        size = self.fill(b, n, part, lengths)
+        stream = torch.cuda.current_stream(self.device)
+        self.start.record(stream)
+        self.inp[:size].copy_(self.inp_host[:size], non_blocking=True)
+        graph.replay()
+        self.out_host[:b].copy_(out, non_blocking=True)
+        self.end.record(stream)
+        self.end.synchronize()
+        return self.out_host[:b].numpy(), self.start.elapsed_time(self.end)
+
+    def _check(self, rows: Sequence[tuple[int, int, Row]]) -> list[int]:
+        loaded = set(self.fast.adapter_index.values())
+        lengths = []
+        for i, (adapter, slot, row) in enumerate(rows):
+            if adapter not in loaded:
+                raise ValueError(f"Row {i}: adapter row {adapter} holds no loaded adapter (loaded rows: "
+                                 f"{sorted(loaded)})")
+            if slot != 0 and self.pool.key(slot) != (adapter, row.prefix_text):
+                raise ValueError(f"Row {i}: prefix slot {slot} holds another prefix than the row's under adapter row "
+                                 f"{adapter} (it holds adapter row {self.pool.key(slot)[0]}'s)")
+            if not 1 <= len(row.new_ids) <= max(C.NEW_BUCKETS):
+                raise ValueError(f"Row {i}: {len(row.new_ids)} new tokens; the batched path takes 1 to "
+                                 f"{max(C.NEW_BUCKETS)}")
+            if not 1 <= row.count <= C.READOUT_ROWS:
+                raise ValueError(f"Row {i}: {row.count} answer options; the readout has 1 to {C.READOUT_ROWS}")
+            lengths.append(self.pool.length(slot))
+        return lengths
+
+    def decide(self, rows: Sequence[tuple[int, int, Row]]) -> tuple[list[list[float]], list[int], dict[str, Any]]:
+        """Each row's option probabilities, input tokens (prefix + new) and timing (batched_path.py:528-562):
+        rows (adapter row, prefix slot, Row) grouped by new-token bucket, passes of at most max_rows(N) rows in the
+        smallest batch bucket that holds them; results in the rows' order."""
+        lengths = self._check(rows)
+        by_bucket: dict[int, list[int]] = {}
+        for i, (_, _, row) in enumerate(rows):
+            by_bucket.setdefault(next(b for b in C.NEW_BUCKETS if b >= len(row.new_ids)), []).append(i)
+        results: list[list[float]] = [[] for _ in rows]
+        batch_rows, bucket, adapters_in_pass = [0] * len(rows), [0] * len(rows), [0] * len(rows)
+        timing: dict[str, Any] = {"model_ms": 0.0, "new_tokens": sum(len(r.new_ids) for _, _, r in rows), "passes": 0}
+        for n, members in sorted(by_bucket.items()):
+            cap = min(max_rows(n), self.ws.rows, self.max_tokens // n)
+            for first in range(0, len(members), cap):
+                part = members[first:first + cap]
+                b = next(bb for bb in C.BATCH_BUCKETS if bb >= len(part))
+                probs, ms = self.run_pass(b, n, [rows[i] for i in part], [lengths[i] for i in part])
+                timing["model_ms"] += ms
+                timing["passes"] += 1
+                adapters = len({rows[i][0] for i in part})
+                for j, i in enumerate(part):
+                    results[i] = probs[j, :rows[i][2].count].tolist()
+                    batch_rows[i], bucket[i], adapters_in_pass[i] = len(part), n, adapters
+        timing.update(batch_rows=batch_rows, bucket=bucket, adapters_in_pass=adapters_in_pass)
+        tokens = [lengths[i] + len(row.new_ids) for i, (_, _, row) in enumerate(rows)]
+        return results, tokens, timing
+
+    # ------------------------------------------------------------ prefixes
+
+    def prefix_passes(self, nb: int, count: int) -> list[int]:
+        """The batch buckets of the passes for `count` new prefixes of bucket nb: largest recorded size first."""
+        cap = min(PREFIX_PASS_ROWS[nb], self.max_tokens // nb, self.ws.rows)
+        sizes = [b for b in C.BATCH_BUCKETS if b <= cap]
+        out = []
+        while count > 0:
+            b = next((s for s in sorted(sizes, reverse=True) if s <= count), None)
+            b = b if b is not None else min(s for s in sizes if s >= count)
+            out.append(b)
+            count -= b
+        return out
+
+    def _prefix_pass(self, b: int, nb: int, part: Sequence[tuple[int, int, list[int]]]) -> float:
+        graph = self.prefix_graph(b, nb)
+        w = self._prefix_width(nb)
+        size = (PREFIX_META + w + nb) * b
+        meta = self.prefix_inp_np[:PREFIX_META * b].reshape(PREFIX_META, b)
+        pages = self.prefix_inp_np[PREFIX_META * b:(PREFIX_META + w) * b].reshape(b, w)
+        ids = self.prefix_inp_np[(PREFIX_META + w) * b:size]
+        meta[:] = 0
+        pages[:] = SINK_PAGE
+        ids[:] = 0
+        for j, (slot, adapter, toks) in enumerate(part):
+            table = self.pool.block_table(slot)
+            if len(toks) > nb or len(table) != self.pool.shapes.pages_per_prefix(len(toks)):
+                raise AssertionError(f"Slot {slot}: a prefix of {len(toks)} tokens with {len(table)} pages staged in a "
+                                     f"pass of {nb}")
+            pages[j, :len(table)] = table
+            ids[j * nb:j * nb + len(toks)] = toks
+            meta[:, j] = (adapter, len(toks))
+        stream = torch.cuda.current_stream(self.device)
+        self.start.record(stream)
+        self.prefix_inp[:size].copy_(self.prefix_inp_host[:size], non_blocking=True)
+        graph.replay()
+        self.end.record(stream)
+        self.end.synchronize()
+        return self.start.elapsed_time(self.end)
+
+    def ensure_prefixes(self, rows: Sequence[tuple[int, str]], max_tokens: int) -> tuple[list[int], dict[str, Any]]:
+        """Each row's prefix slot, pinned once per row (the caller unpins), processing missing prefixes in batched
+        prefix passes (batched_path.py:613-698); on failure every pin of the call is undone and unwritten
+        reservations are released."""
+        pool = self.pool
+        loaded = set(self.fast.adapter_index.values())
+        keys = [(adapter, text) for adapter, text in rows]
+        for i, (adapter, _) in enumerate(keys):
+            if adapter not in loaded:
+                raise ValueError(f"Row {i}: adapter row {adapter} holds no loaded adapter (loaded rows: "
+                                 f"{sorted(loaded)})")
+        new_ids: dict[tuple[int, str], list[int]] = {}
+        for adapter, text in keys:
+            if (adapter, text) in new_ids or pool.lookup(adapter, text) is not None:
+                continue
+            if self.tokenize is None:
+                raise ValueError("This batched path has no tokenizer to process new prefixes")
+            ids = list(self.tokenize(text))
+            if len(ids) > C.LONGEST_PREFIX_TOKENS:
+                raise ValueError(f"The question's fixed part has {len(ids)} tokens; the fast path holds at most "
+                                 f"{C.LONGEST_PREFIX_TOKENS}")
+            if len(ids) >= max_tokens:
+                raise ValueError(f"Question branch exceeds the {max_tokens}-token limit; no input was truncated.")
+            new_ids[(adapter, text)] = ids
+        timing: dict[str, Any] = {"prefix_ms": 0.0, "prefix_misses": len(new_ids), "prefix_hits": 0,
+                                  "prefix_shared": sum(1 for key in keys if key in new_ids) - len(new_ids),
+                                  "prefix_passes": 0}
+        pinned: list[int] = []
+        found: dict[tuple[int, str], int] = {}
+        reserved: dict[tuple[int, str], int] = {}
+        written: set[int] = set()
+        try:
+            for key in keys:
+                if key in new_ids:
+                    continue
+                timing["prefix_hits"] += 1
+                if key not in found:
+                    slot = pool.lookup(*key)
+                    if slot is None:
+                        raise RuntimeError(f"Prefix of adapter row {key[0]} left the pool before any reservation")
+                    pool.pin([slot])
+                    pinned.append(slot)
+                    found[key] = slot
+            for key, ids in new_ids.items():
+                slot = pool.reserve(key[0], key[1], len(ids))
+                reserved[key] = slot
+                pool.pin([slot])
+                pinned.append(slot)
+            slots = [found[key] if key in found else reserved[key] for key in keys]
+            again, seen = [], set()
+            for slot in slots:
+                if slot in seen:
+                    again.append(slot)
+                seen.add(slot)
+            pool.pin(again)
+            pinned.extend(again)
+            by_bucket: dict[int, list[tuple[int, str]]] = {}
+            for key, ids in new_ids.items():
+                nb = next(nb for nb in C.PREFIX_BUCKETS if nb >= max(len(ids), 1))
+                by_bucket.setdefault(nb, []).append(key)
+            for nb, members in sorted(by_bucket.items()):
+                first = 0
+                for b in self.prefix_passes(nb, len(members)):
+                    part = members[first:first + b]
+                    first += b
+                    timing["prefix_ms"] += self._prefix_pass(b, nb, [(reserved[k], k[0], new_ids[k]) for k in part])
+                    timing["prefix_passes"] += 1
+                    written.update(reserved[k] for k in part)
+        except BaseException:
+            pool.unpin(pinned)
+            for slot in reserved.values():
+                if slot not in written:
+                    pool.release(slot)
+            raise
+        return slots, timing

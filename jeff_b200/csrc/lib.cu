@@ -1,0 +1,111 @@
+// libjeffb200: one translation unit (no relocatable device code), host utilities of the C ABI.
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdio.h>
+
+#include <mutex>
+
+#include "common.cuh"
+
+namespace jb {
+
+__device__ int g_device_status;   // set by kernels whose bounded waits gave up (JB_DEV_TIMEOUT | where)
+
+static thread_local char g_error[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+}
+
+int status_of(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return JB_OK;
+  set_error("%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+  return JB_ECUDA;
+}
+
+int check_launch(const char* what) { return status_of(cudaGetLastError(), what); }
+
+int* device_status_word() {
+  static std::mutex mu;
+  static int* addr[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_status) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<int*>(p);
+  }
+  return addr[dev];
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner, uint64_t outer,
+                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return JB_ECUDA;
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15)) {
+    set_error("tensor map: base %p and row pitch %llu must be 16-byte aligned", base, (unsigned long long)row_bytes);
+    return JB_EINVAL;
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t elem[2] = {1, 1};
+  CUresult r = fn(map, dtype, 2, const_cast<void*>(base), dims, strides, box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d): dims %llu x %llu, pitch %llu, box %u x %u", (int)r,
+              (unsigned long long)inner, (unsigned long long)outer, (unsigned long long)row_bytes, box_inner,
+              box_outer);
+    return JB_ECUDA;
+  }
+  return JB_OK;
+}
+
+}  // namespace jb
+
+#include "w4a16_gemm.cu"
+#include "elementwise.cu"
+#include "gdn.cu"
+#include "attention.cu"
+
+extern "C" int jb_abi_version(void) { return 1; }
+
+extern "C" const char* jb_last_error(void) { return jb::g_error; }
+
+extern "C" int jb_device_status(int* status, int reset, void* stream) {
+  JB_REQUIRE(status, "jb_device_status: null status");
+  int* word = jb::device_status_word();
+  if (!word) {
+    jb::set_error("jb_device_status: no device status word on this device");
+    return JB_ECUDA;
+  }
+  cudaStream_t st = (cudaStream_t)stream;
+  int r = jb::status_of(cudaMemcpyAsync(status, word, sizeof(int), cudaMemcpyDeviceToHost, st), "status read");
+  if (r) return r;
+  if (reset) {
+    r = jb::status_of(cudaMemsetAsync(word, 0, sizeof(int), st), "status reset");
+    if (r) return r;
+  }
+  return jb::status_of(cudaStreamSynchronize(st), "status sync");
+}

@@ -1,0 +1,477 @@
+// S1: the int4 W4A16 product fused with the per-row multi-LoRA update, tcgen05 + TMA (sm_100a).
+//
+// y (M, out) = bf16( x (M, K) . W^T + mid . B[a]^T ), W = bf16(fp32(u - z) * fp32(s)) from the reference's int4
+// kernel layout (words (K/8, columns) int32, scales/zeros (K/G, columns) bf16).
+//
+// One CTA computes a 128 x BN tile with 6 warps:
+//   warp 0      TMA producer: per 64-wide K block, the x tile (128 x 64 bf16, 128B swizzle), the packed words
+//               (8 x BN int32) and the group's scale (and zero) rows, into a STAGES-deep ring (mbarrier full[s]);
+//   warp 1      allocates BN TMEM columns; one thread issues tcgen05.mma (M=128, N=BN, K=16) x 4 per K block into
+//               the fp32 accumulator in TMEM and commits each stage back to the producer (empty[s]);
+//   warps 2-5   dequantise each stage's words into bf16 in the UMMA 128B-swizzled K-major layout (deq[s]), then run
+//               the epilogue: the LoRA expand operands (mid rows placed in their adapter's rank block, and the
+//               adapters' B rows) written over the now idle x / weight stages, 1-12 more MMAs into the same
+//               accumulator, TMEM -> registers -> bf16 -> swizzled smem -> TMA store (clipped to M x out).
+// The base product is summed in fp32 in K order; the LoRA term joins the same fp32 accumulator; one rounding at the
+// end: the reference's cut-product rule (int4_kernels.py:1-30). No atomics: the result is deterministic.
+//
+// Dequantisation: nibble pairs become bf16 (128 + u) by OR-ing the exponent bits 0x4300, minus (128 + z) is the
+// exact small integer u - z, times the scale in one bf16 multiply (a single rounding of an exact product), which is
+// bf16(fp32(u - z) * fp32(s)) bit for bit.
+
+namespace jb {
+namespace w4 {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int THREADS = 192;
+constexpr int MAX_EXPAND = 192;   // nA * rank columns of the expand operand (<= 3 swizzle atoms of 64)
+
+struct Params {
+  int M, K, columns, out, group;
+  const __nv_bfloat16* mid;      // (M, rank) or null
+  const __nv_bfloat16* lora_b;   // (pool_rows, columns, rank)
+  const int* adapters;
+  int rank, row_len, pool_rows;
+  int* err;
+};
+
+template <int BN, int STAGES>
+struct Layout {
+  static constexpr int X_BYTES = BM * BK * 2;
+  static constexpr int W_BYTES = BN * BK * 2;
+  static constexpr int RAW_BYTES = 8 * BN * 4;
+  static constexpr int SC_BYTES = BN * 2;
+  static constexpr int OFF_X = 0;
+  static constexpr int OFF_W = OFF_X + STAGES * X_BYTES;
+  static constexpr int OFF_RAW = OFF_W + STAGES * W_BYTES;
+  static constexpr int OFF_SC = OFF_RAW + STAGES * RAW_BYTES;
+  static constexpr int OFF_ZR = OFF_SC + STAGES * SC_BYTES;
+  static constexpr int OFF_BAR = OFF_ZR + STAGES * SC_BYTES;
+  static constexpr int NBAR = 3 * STAGES + 3;
+  static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
+  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int ALLOC = BYTES + 1024;   // room to align the base to 1024 B
+  static_assert(STAGES * X_BYTES >= 3 * 16384 && STAGES * X_BYTES >= BM * BN * 2, "x ring too small to alias");
+  static_assert(STAGES * W_BYTES >= 3 * BN * 128, "weight ring too small to alias");
+};
+
+__device__ __forceinline__ uint32_t pair_bits(uint32_t w, int pair) {
+  // nibbles 2p and 2p+1 of w into the low bits of the two bf16 halves
+  uint32_t lo = (w >> (8 * pair)) & 0xFu;
+  uint32_t hi = (w >> (8 * pair + 4)) & 0xFu;
+  return lo | (hi << 16) | 0x43004300u;
+}
+
+// 8 weights of one word: bf16((u - z) * s) for u the 8 nibbles (input order), s2 = {s, s}, zb2 = {128 + z, 128 + z}
+__device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 zb2) {
+  uint32_t r[4];
+#pragma unroll
+  for (int p = 0; p < 4; ++p) {
+    uint32_t t = pair_bits(w, p);
+    __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&t);
+    v = __hmul2(__hsub2(v, zb2), s2);
+    r[p] = *reinterpret_cast<uint32_t*>(&v);
+  }
+  return make_uint4(r[0], r[1], r[2], r[3]);
+}
+
+__device__ __forceinline__ __nv_bfloat162 zero_pair(const __nv_bfloat16* zr, int n) {
+  float z = zr ? __bfloat162float(zr[n]) : 8.0f;
+  return __floats2bfloat162_rn(128.0f + z, 128.0f + z);
+}
+
+template <int BN, int STAGES, bool ZERO>
+__global__ void __launch_bounds__(THREADS, 1)
+    w4a16_lora_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                      const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
+                      const __grid_constant__ CUtensorMap tm_y, Params p) {
+  using L = Layout<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* full = bars;
+  uint64_t* deq = bars + STAGES;
+  uint64_t* empty = bars + 2 * STAGES;
+  uint64_t* main_done = bars + 3 * STAGES;
+  uint64_t* lora_ready = main_done + 1;
+  uint64_t* acc_full = main_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
+  volatile int* epi_ok = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * BM;
+  const int n0 = blockIdx.y * BN;
+  const int nkb = p.K / BK;
+  const bool has_lora = p.mid != nullptr && p.rank > 0;
+  const int n_adp = p.row_len >= BM ? 1 : BM / p.row_len;
+  const int ke = has_lora ? n_adp * p.rank : 0;   // expand K (multiple of 16)
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&deq[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(main_done, 1);
+    mbar_init(lora_ready, 1);
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    *epi_ok = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    prefetch_tmap(&tm_x);
+    prefetch_tmap(&tm_w);
+    prefetch_tmap(&tm_s);
+    if (ZERO) prefetch_tmap(&tm_z);
+    prefetch_tmap(&tm_y);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, BN);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const uint32_t bytes = L::X_BYTES + L::RAW_BYTES + L::SC_BYTES * (ZERO ? 2 : 1);
+      for (int kb = 0; kb < nkb; ++kb) {
+        const int s = kb % STAGES;
+        if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort_flag, p.err, 1)) break;
+        mbar_arrive_expect_tx(&full[s], bytes);
+        tma_load_2d(smem + L::OFF_X + s * L::X_BYTES, &tm_x, &full[s], kb * BK, m0);
+        tma_load_2d(smem + L::OFF_RAW + s * L::RAW_BYTES, &tm_w, &full[s], n0, kb * (BK / 8));
+        tma_load_2d(smem + L::OFF_SC + s * L::SC_BYTES, &tm_s, &full[s], n0, (kb * BK) / p.group);
+        if (ZERO) tma_load_2d(smem + L::OFF_ZR + s * L::SC_BYTES, &tm_z, &full[s], n0, (kb * BK) / p.group);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16(BM, BN);
+      bool ok = true;
+      for (int kb = 0; kb < nkb && ok; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        ok = mbar_wait(&full[s], ph, abort_flag, p.err, 2) && mbar_wait(&deq[s], ph, abort_flag, p.err, 3);
+        if (!ok) break;
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES));
+        const uint64_t bd = sw128_desc(smem_u32(smem + L::OFF_W + s * L::W_BYTES));
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; ++kk) tc_mma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+        tc_commit(&empty[s]);
+      }
+      tc_commit(main_done);
+      if (ok && mbar_wait(lora_ready, 0, abort_flag, p.err, 4)) {
+        tc_fence_after();
+        for (int j = 0; j < ke / 16; ++j) {
+          const int atom = j >> 2, w16 = j & 3;
+          const uint64_t ad = sw128_desc(smem_u32(smem + L::OFF_X + atom * 16384)) + 2 * w16;
+          const uint64_t bd = sw128_desc(smem_u32(smem + L::OFF_W + atom * BN * 128)) + 2 * w16;
+          tc_mma_bf16(tmem, ad, bd, idesc, 1);
+        }
+      }
+      tc_commit(acc_full);
+    }
+  } else {
+    // ---------------- dequantisers, then the epilogue: 128 threads
+    const int et = threadIdx.x - 64;
+    for (int kb = 0; kb < nkb; ++kb) {
+      const int s = kb % STAGES;
+      const bool ok = mbar_wait(&full[s], (kb / STAGES) & 1, abort_flag, p.err, 5);
+      if (!__all_sync(0xffffffffu, ok)) break;
+      const int32_t* raw = reinterpret_cast<const int32_t*>(smem + L::OFF_RAW + s * L::RAW_BYTES);
+      const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(smem + L::OFF_SC + s * L::SC_BYTES);
+      const __nv_bfloat16* zr = ZERO ? reinterpret_cast<const __nv_bfloat16*>(smem + L::OFF_ZR + s * L::SC_BYTES)
+                                     : nullptr;
+      uint8_t* wt = smem + L::OFF_W + s * L::W_BYTES;
+#pragma unroll
+      for (int nn = 0; nn < BN / 128; ++nn) {
+        const int n = et + nn * 128;
+        const __nv_bfloat162 s2 = __bfloat162bfloat162(sc[n]);
+        const __nv_bfloat162 zb2 = zero_pair(zr, n);
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const uint4 v = dequant8(static_cast<uint32_t>(raw[r * BN + n]), s2, zb2);
+          *reinterpret_cast<uint4*>(wt + sw128_offset(n, r)) = v;
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&deq[s]);
+    }
+
+    // ---------------- epilogue
+    const int row = 32 * (warp & 3) + lane;   // the TMEM lane this thread may read
+    if (et == 0) *epi_ok = mbar_wait(main_done, 0, abort_flag, p.err, 6) ? 1 : 0;
+    named_barrier(1, 128);
+    const bool go = *epi_ok != 0;
+    if (go && has_lora) {
+      // mid rows into their adapter block of the expand A operand (over the x ring; all x stages are consumed)
+      const int ke_pad = (ke + 63) & ~63;
+      const int gm = m0 + row;
+      const int block_of_row = (p.row_len >= BM) ? 0 : (row / p.row_len);
+      uint8_t* mid_t = smem + L::OFF_X;
+      for (int c8 = 0; c8 < ke_pad / 8; ++c8) {
+        const int col = c8 * 8;
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (col < ke && gm < p.M && col / p.rank == block_of_row)
+          v = *reinterpret_cast<const uint4*>(p.mid + (size_t)gm * p.rank + (col % p.rank));
+        *reinterpret_cast<uint4*>(mid_t + (col >> 6) * 16384 + sw128_offset(row, (col & 63) >> 3)) = v;
+      }
+      // the tile's adapters' B rows (over the weight ring)
+      uint8_t* b_t = smem + L::OFF_W;
+      const int first_row_block = m0 / p.row_len;
+      for (int nn = 0; nn < BN / 128; ++nn) {
+        const int n = et + nn * 128;
+        const int gn = n0 + n;
+        for (int c8 = 0; c8 < ke_pad / 8; ++c8) {
+          const int col = c8 * 8;
+          uint4 v = make_uint4(0, 0, 0, 0);
+          const int blk = col / p.rank;
+          if (col < ke && gn < p.columns && (first_row_block + blk) * p.row_len < p.M) {
+            int a = p.adapters[first_row_block + blk];
+            if (a >= 0 && a < p.pool_rows)
+              v = *reinterpret_cast<const uint4*>(p.lora_b + ((size_t)a * p.columns + gn) * p.rank + (col % p.rank));
+          }
+          *reinterpret_cast<uint4*>(b_t + (col >> 6) * (BN * 128) + sw128_offset(n, (col & 63) >> 3)) = v;
+        }
+      }
+      fence_proxy_async_smem();
+    }
+    named_barrier(1, 128);
+    if (et == 0) mbar_arrive(lora_ready);
+    if (et == 0) *epi_ok = (go && mbar_wait(acc_full, 0, abort_flag, p.err, 7)) ? 1 : 0;
+    named_barrier(1, 128);
+    if (*epi_ok) {
+      tc_fence_after();
+      uint8_t* out_t = smem + L::OFF_X;
+      const uint32_t lane_addr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(lane_addr + c * 32, r);
+        tc_wait_ld();
+        const int half = (c * 32) >> 6;
+        const int chunk0 = ((c * 32) & 63) >> 3;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint4 v;
+          v.x = pack_bf2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+          v.y = pack_bf2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+          v.z = pack_bf2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+          v.w = pack_bf2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+          *reinterpret_cast<uint4*>(out_t + half * 16384 + sw128_offset(row, chunk0 + q)) = v;
+        }
+      }
+      fence_proxy_async_smem();
+      named_barrier(1, 128);
+      if (et == 0) {
+        for (int h = 0; h < BN / 64; ++h)
+          if (n0 + h * 64 < p.out) tma_store_2d(&tm_y, out_t + h * 16384, n0 + h * 64, m0);
+        tma_store_commit_and_wait();
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, BN);
+  }
+}
+
+// ------------------------------------------------------------------ LoRA first factor (mma.sync, small)
+
+template <int NB>   // rank / 8 output blocks
+__global__ void __launch_bounds__(128) lora_shrink_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
+                                                          const __nv_bfloat16* __restrict__ A, int pool_rows,
+                                                          const int* __restrict__ adapters, int row_len,
+                                                          __nv_bfloat16* __restrict__ mid) {
+  constexpr int R = NB * 8;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = (blockIdx.x * 4 + warp) * 16;
+  if (m0 >= M) return;
+  int a = adapters[m0 / row_len];
+  if (a < 0 || a >= pool_rows) a = 0;
+  const __nv_bfloat16* Aa = A + (size_t)a * R * K;
+  const int g = lane >> 2, t = lane & 3;
+  float acc[NB][4];
+#pragma unroll
+  for (int i = 0; i < NB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  const __nv_bfloat16* x0 = x + (size_t)(m0 + g) * K;
+  const __nv_bfloat16* x1 = x0 + (size_t)8 * K;
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    const uint32_t a0 = *reinterpret_cast<const uint32_t*>(x0 + k0 + 2 * t);
+    const uint32_t a1 = *reinterpret_cast<const uint32_t*>(x1 + k0 + 2 * t);
+    const uint32_t a2 = *reinterpret_cast<const uint32_t*>(x0 + k0 + 8 + 2 * t);
+    const uint32_t a3 = *reinterpret_cast<const uint32_t*>(x1 + k0 + 8 + 2 * t);
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const __nv_bfloat16* brow = Aa + (size_t)(nb * 8 + g) * K + k0;
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(brow + 2 * t);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(brow + 8 + 2 * t);
+      asm volatile(
+          "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+          "{%0, %1, %2, %3};"
+          : "+f"(acc[nb][0]), "+f"(acc[nb][1]), "+f"(acc[nb][2]), "+f"(acc[nb][3])
+          : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+    }
+  }
+#pragma unroll
+  for (int nb = 0; nb < NB; ++nb) {
+    const int col = nb * 8 + 2 * t;
+    *reinterpret_cast<uint32_t*>(mid + (size_t)(m0 + g) * R + col) = pack_bf2(acc[nb][0], acc[nb][1]);
+    *reinterpret_cast<uint32_t*>(mid + (size_t)(m0 + g + 8) * R + col) = pack_bf2(acc[nb][2], acc[nb][3]);
+  }
+}
+
+// ------------------------------------------------------------------ standalone dequantiser (verification)
+
+__global__ void int4_dequant_kernel(const int32_t* __restrict__ words, const __nv_bfloat16* __restrict__ scales,
+                                    const __nv_bfloat16* __restrict__ zeros, int K, int columns, int group,
+                                    __nv_bfloat16* __restrict__ out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int i = blockIdx.y;   // word row: inputs 8i .. 8i + 7
+  if (c >= columns) return;
+  const int gi = (8 * i) / group;
+  const __nv_bfloat162 s2 = __bfloat162bfloat162(scales[(size_t)gi * columns + c]);
+  const float z = zeros ? __bfloat162float(zeros[(size_t)gi * columns + c]) : 8.0f;
+  const __nv_bfloat162 zb2 = __floats2bfloat162_rn(128.0f + z, 128.0f + z);
+  const uint4 v = dequant8(static_cast<uint32_t>(words[(size_t)i * columns + c]), s2, zb2);
+  *reinterpret_cast<uint4*>(out + (size_t)c * K + 8 * i) = v;
+}
+
+template <int BN, int STAGES, bool ZERO>
+int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz,
+           const CUtensorMap& ty, const Params& p, cudaStream_t stream) {
+  using L = Layout<BN, STAGES>;
+  auto kernel = w4a16_lora_kernel<BN, STAGES, ZERO>;
+  static bool configured[8] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 8 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+    if (e != cudaSuccess) return status_of(e, "w4a16: cudaFuncSetAttribute");
+    configured[dev] = true;
+  }
+  dim3 grid((p.M + BM - 1) / BM, (p.columns + BN - 1) / BN);
+  kernel<<<grid, THREADS, L::ALLOC, stream>>>(tx, tw, ts, tz, ty, p);
+  return check_launch("w4a16_lora_kernel");
+}
+
+}  // namespace w4
+}  // namespace jb
+
+using namespace jb;
+
+extern "C" int jb_int4_dequant(const int32_t* words, const uint16_t* scales, const uint16_t* zeros, int k,
+                               int columns, int group, uint16_t* out, void* stream) {
+  JB_REQUIRE(words && scales && out, "jb_int4_dequant: null pointer");
+  JB_REQUIRE(k > 0 && k % 64 == 0 && columns > 0 && columns % 64 == 0,
+             "jb_int4_dequant: k (%d) and columns (%d) must be positive multiples of 64", k, columns);
+  JB_REQUIRE(group == 64 || group == 128, "jb_int4_dequant: group %d (64 or 128)", group);
+  JB_REQUIRE(k % group == 0, "jb_int4_dequant: k %d is not a multiple of the group %d", k, group);
+  dim3 grid((columns + 127) / 128, k / 8);
+  w4::int4_dequant_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(
+      words, reinterpret_cast<const __nv_bfloat16*>(scales), reinterpret_cast<const __nv_bfloat16*>(zeros), k,
+      columns, group, reinterpret_cast<__nv_bfloat16*>(out));
+  return check_launch("int4_dequant_kernel");
+}
+
+extern "C" int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* lora_a, int rank, int pool_rows,
+                              const int32_t* adapters, int row_len, uint16_t* mid, void* stream) {
+  JB_REQUIRE(x && lora_a && adapters && mid, "jb_lora_shrink: null pointer");
+  JB_REQUIRE(m > 0 && m % 16 == 0, "jb_lora_shrink: m %d must be a positive multiple of 16", m);
+  JB_REQUIRE(k > 0 && k % 16 == 0, "jb_lora_shrink: k %d must be a positive multiple of 16", k);
+  JB_REQUIRE(row_len > 0 && row_len % 16 == 0, "jb_lora_shrink: row_len %d must be a multiple of 16", row_len);
+  JB_REQUIRE(pool_rows > 0, "jb_lora_shrink: pool_rows %d", pool_rows);
+  dim3 grid((m / 16 + 3) / 4);
+  auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
+  auto ab = reinterpret_cast<const __nv_bfloat16*>(lora_a);
+  auto mb = reinterpret_cast<__nv_bfloat16*>(mid);
+  cudaStream_t st = (cudaStream_t)stream;
+  switch (rank) {
+    case 16: w4::lora_shrink_kernel<2><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
+    case 32: w4::lora_shrink_kernel<4><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
+    case 48: w4::lora_shrink_kernel<6><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
+    case 64: w4::lora_shrink_kernel<8><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
+    default: set_error("jb_lora_shrink: rank %d (16, 32, 48 or 64)", rank); return JB_EINVAL;
+  }
+  return check_launch("lora_shrink_kernel");
+}
+
+extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
+                             const uint16_t* zeros, int group, int columns, int out, const uint16_t* mid,
+                             const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
+                             uint16_t* y, int ldy, void* stream) {
+  JB_REQUIRE(x && words && scales && y, "jb_w4a16_lora: null pointer");
+  JB_REQUIRE(m > 0 && k > 0 && k % 64 == 0, "jb_w4a16_lora: m %d, k %d (k a multiple of 64)", m, k);
+  JB_REQUIRE(columns > 0 && columns % 64 == 0 && out > 0 && out <= columns,
+             "jb_w4a16_lora: columns %d (multiple of 64), out %d <= columns", columns, out);
+  JB_REQUIRE(group == 64 || group == 128, "jb_w4a16_lora: group %d (64 or 128)", group);
+  JB_REQUIRE(ldy >= out && ldy % 8 == 0, "jb_w4a16_lora: ldy %d must be >= out and a multiple of 8", ldy);
+  JB_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 &&
+                 (reinterpret_cast<uintptr_t>(words) & 15) == 0 && (reinterpret_cast<uintptr_t>(scales) & 15) == 0,
+             "jb_w4a16_lora: x, y, words and scales must be 16-byte aligned");
+  const bool lora = mid != nullptr && rank > 0;
+  if (lora) {
+    JB_REQUIRE(lora_b && adapters, "jb_w4a16_lora: LoRA needs lora_b and adapters");
+    JB_REQUIRE(rank % 16 == 0 && rank <= 64, "jb_w4a16_lora: rank %d (16, 32, 48 or 64)", rank);
+    JB_REQUIRE(row_len > 0 && row_len % 32 == 0 && (row_len % w4::BM == 0 || w4::BM % row_len == 0),
+               "jb_w4a16_lora: row_len %d must be a multiple of 32 that divides or is divided by 128", row_len);
+    const int n_adp = row_len >= w4::BM ? 1 : w4::BM / row_len;
+    JB_REQUIRE(n_adp * rank <= w4::MAX_EXPAND, "jb_w4a16_lora: %d adapters per tile x rank %d exceeds %d", n_adp,
+               rank, w4::MAX_EXPAND);
+    JB_REQUIRE(pool_rows > 0, "jb_w4a16_lora: pool_rows %d", pool_rows);
+  }
+  CUtensorMap tx, tw, ts, tz, ty;
+  int st;
+  constexpr int BN = 128;
+  if ((st = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, m, (uint64_t)k * 2, 64, w4::BM,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  if ((st = make_tmap_2d(&tw, words, CU_TENSOR_MAP_DATA_TYPE_INT32, columns, k / 8, (uint64_t)columns * 4, BN, 8,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return st;
+  if ((st = make_tmap_2d(&ts, scales, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, columns, k / group, (uint64_t)columns * 2,
+                         BN, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return st;
+  if (zeros) {
+    JB_REQUIRE((reinterpret_cast<uintptr_t>(zeros) & 15) == 0, "jb_w4a16_lora: zeros must be 16-byte aligned");
+    if ((st = make_tmap_2d(&tz, zeros, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, columns, k / group, (uint64_t)columns * 2,
+                           BN, 1, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      return st;
+  } else {
+    tz = ts;
+  }
+  if ((st = make_tmap_2d(&ty, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, m, (uint64_t)ldy * 2, 64, w4::BM,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
+  w4::Params p{m, k, columns, out, group,
+               lora ? reinterpret_cast<const __nv_bfloat16*>(mid) : nullptr,
+               reinterpret_cast<const __nv_bfloat16*>(lora_b), adapters, lora ? rank : 0, row_len > 0 ? row_len : 128,
+               pool_rows, device_status_word()};
+  if (zeros) return w4::launch<BN, 5, true>(tx, tw, ts, tz, ty, p, (cudaStream_t)stream);
+  return w4::launch<BN, 5, false>(tx, tw, ts, tz, ty, p, (cudaStream_t)stream);
+}
+
+extern "C" int jb_int4_lora_product(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
+                                    const uint16_t* zeros, int group, int columns, int out, const uint16_t* lora_a,
+                                    const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters,
+                                    int row_len, uint16_t* mid, uint16_t* y, int ldy, void* stream) {
+  if (rank > 0) {
+    JB_REQUIRE(mid && lora_a, "jb_int4_lora_product: LoRA needs lora_a and the mid scratch");
+    int st = jb_lora_shrink(x, m, k, lora_a, rank, pool_rows, adapters, row_len, mid, stream);
+    if (st) return st;
+  }
+  return jb_w4a16_lora(x, m, k, words, scales, zeros, group, columns, out, rank > 0 ? mid : nullptr, lora_b, rank,
+                       pool_rows, adapters, row_len, y, ldy, stream);
+}

@@ -1,0 +1,360 @@
+"""Each CUDA kernel of the hot path against the CPU oracle on the same seeded inputs (B200 only), in passes of
+B = 1, 3 and 16 rows whose prefixes have mixed lengths (0, and lengths that are not multiples of 32), read through
+block tables from a real prefix pool whose pages hold NaN past each prefix's end, so a read out of bounds shows up.
+
+Tolerances follow the reference's kernel tests (runtime/python/tests/test_batched_kernels.py) and are stated per test:
+one bfloat16 step is 2^-7 of the value at most; references that round the same values can land a step apart when
+their float32 sums differ in the last bits. Integer work (unpack, dequantise) is bit-exact."""
+
+from __future__ import annotations
+
+import math
+import random
+
+import numpy as np
+import pytest
+import torch
+
+from jeff_b200 import constants as C
+from jeff_b200 import int4 as prod_int4
+from jeff_b200 import kernels, synthetic
+from jeff_b200.prefix_pool import PrefixPool
+from oracle import int4_ref, model_ref
+
+pytestmark = pytest.mark.gpu
+
+BF16_STEP = 2.0 ** -7
+PREFIX_LENGTHS = (0, 1, 7, 31, 32, 33, 45, 64, 100, 257, 513, 1000)
+BATCHES = (1, 3, 16)
+
+
+def bf(x: torch.Tensor) -> torch.Tensor:
+    return x.to(torch.bfloat16).float()
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+@pytest.fixture(scope="module")
+def pool_fixture():
+    """A pool with one random prefix per length (NaN past each prefix's end in its last key/value page), and the
+    CPU copies of every prefix's state."""
+    torch.manual_seed(0)
+    pool = PrefixPool(2 + 60 * len(PREFIX_LENGTHS) + 200, "cuda")
+    shapes = pool.shapes
+    slots, states = {}, {}
+    for i, p in enumerate(PREFIX_LENGTHS):
+        slot = pool.reserve(1, f"prefix {i}", p)
+        padded = math.ceil(p / 32) * 32
+        kv = torch.randn(shapes.attn_layers, 2, padded, *shapes.kv).to(torch.bfloat16)
+        kv[:, :, p:] = float("nan")
+        conv = torch.randn(shapes.gdn_layers, *shapes.conv).to(torch.bfloat16)
+        state = 0.5 * torch.randn(shapes.gdn_layers, *shapes.state)
+        pool.write(slot, conv.cuda(), state.cuda(), kv.cuda())
+        # write() pads partial pages with zeros: poison the tail of the last page explicitly
+        if p % 32:
+            table = pool.block_table(slot)
+            last_page = table[shapes.fixed_pages + p // 32]
+            pool.kv[last_page, :, :, p % 32:] = float("nan")
+        slots[p] = slot
+        states[slot] = (conv, state, kv[:, :, :p])
+    states[0] = (torch.zeros(shapes.gdn_layers, *shapes.conv), torch.zeros(shapes.gdn_layers, *shapes.state),
+                 torch.zeros(shapes.attn_layers, 2, 0, *shapes.kv))
+    return pool, slots, states
+
+
+def pass_slots(slots: dict[int, int], b: int, seed: int) -> list[int]:
+    if b == 1:
+        return [slots[33]]
+    must = [0, slots[0], slots[33], slots[32], slots[1000]]
+    rng = random.Random(seed)
+    every = [0, *slots.values()]
+    chosen = (must + [rng.choice(every) for _ in range(b)])[:b]
+    rng.shuffle(chosen)
+    return chosen
+
+
+def tables_for(pool: PrefixPool, slots: list[int]) -> tuple[torch.Tensor, torch.Tensor]:
+    idx = torch.tensor(slots, device="cuda")
+    tables = pool.tables.index_select(0, idx).contiguous()
+    pos = torch.tensor([pool.length(s) for s in slots], device="cuda", dtype=torch.int32)
+    return tables, pos
+
+
+# ---------------------------------------------------------------- int4
+
+
+@pytest.mark.parametrize("fmt", ["g64", "g128z"])
+def test_int4_dequant_is_bit_exact(fmt: str) -> None:
+    w = synthetic.normal(7, f"dq/{fmt}", (330, 512), 0.02)
+    packed, _ = prod_int4.quantize_pack(w, fmt)
+    dev = packed.to("cuda")
+    got = kernels.int4_dequant(dev.words, dev.scales, dev.zeros, packed.group)
+    zb = None if packed.zeros is None else bits(packed.zeros)
+    want = int4_ref.dequantize_kernel_layout(packed.words.numpy(), bits(packed.scales), zb, packed.group)
+    assert np.array_equal(bits(got), want)
+
+
+def exact_product(x: torch.Tensor, W: torch.Tensor, a_rows, b_rows, row_of: torch.Tensor):
+    """float64 exact x W^T + bf16(x A^T) B^T per row, and the forward-error bound of a product rounded once
+    (one bf16 step of the result, the float32 accumulation slack over k + rank terms, the mid's bf16 rounding)."""
+    xd = x.double()
+    exact = xd @ W.double().T
+    mag = xd.abs() @ W.double().abs().T
+    lora_round = torch.zeros_like(exact)
+    for r in torch.unique(row_of).tolist():
+        sel = row_of == r
+        a, b = a_rows[r].double(), b_rows[r].double()
+        mid = xd[sel] @ a.T
+        exact[sel] += bf(mid.float()).double() @ b.T
+        mag[sel] += (xd[sel].abs() @ a.abs().T) @ b.abs().T
+        lora_round[sel] = 2.0 ** -9 * (mid.abs() @ b.abs().T)
+    k = x.shape[1] + a_rows[0].shape[0]
+    _, e = torch.frexp(exact.abs())
+    step = torch.where(exact == 0, torch.zeros_like(exact), torch.ldexp(torch.ones_like(exact), e - 8))
+    return exact, step + k * 2.0 ** -23 * mag + lora_round
+
+
+@pytest.mark.parametrize("fmt", ["g128z", "g64"])
+@pytest.mark.parametrize(("m", "k", "outs", "row_len"), [
+    (64, 1024, [3584], 64),                       # configuration 1
+    (128, 1024, [6144, 2048, 16, 16], 32),        # the Gated DeltaNet projection, 4 adapters per tile
+    (256, 1024, [4096, 512, 512], 128),           # the attention projection (q+gate, k, v)
+    (192, 2048, [1024], 64),                      # out_proj, ragged M (not a multiple of 128)
+    (96, 3584, [1024], 32),                       # down_proj, k = 3584
+])
+def test_int4_lora_product_within_its_error_bound(fmt: str, m: int, k: int, outs: list[int], row_len: int) -> None:
+    g = torch.Generator().manual_seed(m + k + len(outs))
+    w = torch.randn(sum(outs), k, generator=g) * 0.02
+    packed, W = prod_int4.quantize_pack(w, fmt)
+    rank = 16 * min(len(outs), 3)
+    rows = m // row_len
+    pool_rows = 5
+    a_pool = (torch.randn(pool_rows, rank, k, generator=g) * 0.02).to(torch.bfloat16)
+    b_pool = torch.zeros(pool_rows, packed.columns, rank, dtype=torch.bfloat16)
+    b_pool[:, :sum(outs)] = (torch.randn(pool_rows, sum(outs), rank, generator=g) * 0.02).to(torch.bfloat16)
+    a_pool[0] = 0
+    b_pool[0] = 0
+    adapters = torch.randint(0, pool_rows, (rows,), generator=g, dtype=torch.int32)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    dev = packed.to("cuda")
+    got = kernels.int4_product(x.cuda(), dev.words, dev.scales, dev.zeros, packed.group, sum(outs), a_pool.cuda(),
+                               b_pool.cuda(), adapters.cuda(), row_len).cpu()
+    row_of = adapters.long().repeat_interleave(row_len)
+    exact, bound = exact_product(x.float(), W.float(), a_pool.float(), b_pool[:, :sum(outs)].float(), row_of)
+    err = (got.double() - exact).abs()
+    assert int((err > bound).sum()) == 0, f"worst at {(err / bound.clamp_min(1e-30)).max():.3g} x the bound"
+    # and the same bits on a second run (no atomics: deterministic)
+    again = kernels.int4_product(x.cuda(), dev.words, dev.scales, dev.zeros, packed.group, sum(outs), a_pool.cuda(),
+                                 b_pool.cuda(), adapters.cuda(), row_len).cpu()
+    assert torch.equal(got, again)
+
+
+def test_lora_shrink_matches_the_oracle() -> None:
+    g = torch.Generator().manual_seed(3)
+    m, k, rank = 256, 1024, 48
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    a_pool = (torch.randn(3, rank, k, generator=g) * 0.02).to(torch.bfloat16)
+    adapters = torch.tensor([2, 0, 1, 2], dtype=torch.int32)
+    got = kernels.lora_shrink(x.cuda(), a_pool.cuda(), adapters.cuda(), 64).cpu().float()
+    row_of = adapters.long().repeat_interleave(64)
+    want = torch.stack([x[i].float() @ a_pool[row_of[i]].float().T for i in range(m)])
+    torch.testing.assert_close(got, bf(want), rtol=BF16_STEP, atol=1e-6)
+
+
+# ---------------------------------------------------------------- norms and activations
+
+
+def test_add_rms_and_rms_last_match_the_oracle() -> None:
+    g = torch.Generator().manual_seed(4)
+    x = torch.randn(96, 1024, generator=g).to(torch.bfloat16)
+    d = torch.randn(96, 1024, generator=g).to(torch.bfloat16)
+    w = torch.randn(1024, generator=g) * 0.1
+    xo, h = kernels.add_rms(x.cuda(), d.cuda(), (1.0 + w).cuda())
+    rx, rh = model_ref.add_rms(x.float(), d.float(), w)
+    assert torch.equal(xo.cpu().float(), rx)     # one rounding of an exact sum
+    torch.testing.assert_close(h.cpu().float(), rh, rtol=BF16_STEP, atol=1e-6)
+    _, h0 = kernels.add_rms(x.cuda(), None, (1.0 + w).cuda())
+    torch.testing.assert_close(h0.cpu().float(), model_ref.add_rms(x.float(), None, w)[1], rtol=BF16_STEP, atol=1e-6)
+    last = torch.tensor([31, 0, 17], dtype=torch.int32)
+    hid = kernels.rms_last(x.cuda(), d.cuda(), last.cuda(), 32, (1.0 + w).cuda()).cpu().float()
+    at = torch.arange(3) * 32 + last.long()
+    _, want = model_ref.add_rms(bf(x[at].float() + d[at].float()), None, w)
+    torch.testing.assert_close(hid, want, rtol=BF16_STEP, atol=1e-6)
+
+
+def test_activations_match_the_oracle() -> None:
+    g = torch.Generator().manual_seed(5)
+    gu = torch.randn(64, 2 * C.INTER, generator=g).to(torch.bfloat16)
+    torch.testing.assert_close(kernels.silu_mul(gu.cuda()).cpu().float(), model_ref.silu_mul(gu.float()),
+                               rtol=BF16_STEP, atol=1e-6)
+    pr = torch.randn(64, C.ATTN_PROJ, generator=g).to(torch.bfloat16)
+    o = torch.randn(64, C.NQ, C.HD, generator=g).to(torch.bfloat16)
+    gate = pr.float()[:, :C.NQ * 2 * C.HD].view(64, C.NQ, 2 * C.HD)[:, :, C.HD:]
+    torch.testing.assert_close(kernels.gate_mul(o.cuda(), pr.cuda()).cpu().float(),
+                               model_ref.gate_mul(o.float(), gate), rtol=BF16_STEP, atol=1e-6)
+    prg = torch.randn(64, C.GDN_PROJ, generator=g).to(torch.bfloat16)
+    og = (0.3 * torch.randn(64, C.NV, C.DV, generator=g)).to(torch.bfloat16)
+    wg = (1 + 0.1 * torch.randn(C.DV, generator=g)).to(torch.bfloat16)
+    torch.testing.assert_close(kernels.gated_norm(og.cuda(), prg.cuda(), wg.cuda()).cpu().float(),
+                               model_ref.gated_norm(og.float(), prg[:, C.QKV_DIM:C.QKV_DIM + C.Z_DIM], wg),
+                               rtol=2 * BF16_STEP, atol=1e-5)
+    table = torch.randn(500, 1024, generator=g).to(torch.bfloat16)
+    ids = torch.randint(0, 500, (77,), generator=g, dtype=torch.int32)
+    assert torch.equal(kernels.embed(table.cuda(), ids.cuda()).cpu(), table[ids.long()])
+
+
+@pytest.mark.parametrize("b", BATCHES)
+def test_readout_rows_match_the_oracle(b: int) -> None:
+    g = torch.Generator().manual_seed(b)
+    rng = random.Random(b)
+    hidden = torch.randn(b, 1024, generator=g).to(torch.bfloat16)
+    pool = (0.05 * torch.randn(6, 255, 1024, generator=g)).to(torch.bfloat16)
+    temps = 0.5 + 1.5 * torch.rand(6, generator=g)
+    adapters = torch.tensor([rng.randrange(6) for _ in range(b)], dtype=torch.int32)
+    counts = torch.tensor(([1, 2, 255] + [rng.randrange(1, 256) for _ in range(b)])[:b], dtype=torch.int32)
+    got = kernels.readout_rows(hidden.cuda(), pool.cuda(), temps.cuda(), adapters.cuda(), counts.cuda()).cpu()
+    for r in range(b):
+        want = model_ref.readout(hidden[r].float(), pool[adapters[r]], int(counts[r]), float(temps[adapters[r]]))
+        torch.testing.assert_close(got[r], want, rtol=1e-3, atol=1e-5)
+        assert not got[r, int(counts[r]):].any()
+
+
+# ---------------------------------------------------------------- Gated DeltaNet
+
+
+@pytest.mark.parametrize("b", BATCHES)
+@pytest.mark.parametrize("n", [32, 64])
+@pytest.mark.parametrize("gdn_layer", [0, 13, 17])
+def test_gdn_prep_rows_match_the_oracle(pool_fixture, b: int, n: int, gdn_layer: int) -> None:
+    """q, k within two bf16 steps (the L2 norm's sum order), v and beta within one, g float32 within 1e-5."""
+    pool, slots, states = pool_fixture
+    ss = pass_slots(slots, b, seed=b * 100 + n + gdn_layer)
+    tables, _ = tables_for(pool, ss)
+    g = torch.Generator().manual_seed(gdn_layer)
+    conv_w = bf(0.5 * torch.randn(4, C.QKV_DIM, generator=g)).contiguous()
+    a_log = torch.randn(C.NV, generator=g)
+    dt_bias = torch.randn(C.NV, generator=g)
+    pr = torch.randn(b * n, C.GDN_PROJ, generator=g).to(torch.bfloat16)
+    got = kernels.gdn_prep_rows(pr.cuda(), pool, tables, gdn_layer, conv_w.cuda(), (-torch.exp(a_log)).cuda(),
+                                dt_bias.cuda(), n)
+    for r in range(b):
+        tail = states[ss[r]][0][gdn_layer]
+        want = model_ref.gdn_prep(pr[r * n:(r + 1) * n], tail, conv_w.T, a_log, dt_bias)
+        for name, x, y, rtol in zip("q k v".split(), got[:3], want[:3], (2 * BF16_STEP, 2 * BF16_STEP, BF16_STEP),
+                                    strict=True):
+            torch.testing.assert_close(x[r].cpu().float(), y, rtol=rtol, atol=1e-6, msg=lambda m, nm=name: f"{nm}: {m}")
+        torch.testing.assert_close(got[3][r].cpu(), want[3], rtol=1e-5, atol=1e-6)
+        torch.testing.assert_close(got[4][r].cpu().float(), want[4], rtol=BF16_STEP, atol=1e-6)
+
+
+GDN_RTOL, GDN_ATOL = 2.0 ** -6, 2.0 ** -9
+
+
+def gdn_inputs(b: int, n: int, seed: int):
+    g = torch.Generator().manual_seed(seed)
+
+    def unit() -> torch.Tensor:
+        x = torch.randn(b, n, C.NV, C.DK, generator=g)
+        return (x / x.norm(dim=-1, keepdim=True)).to(torch.bfloat16)
+
+    q, k = unit(), unit()
+    v = torch.randn(b, n, C.NV, C.DV, generator=g).to(torch.bfloat16)
+    gg = -0.5 * torch.nn.functional.softplus(torch.randn(b, n, C.NV, generator=g))
+    beta = torch.sigmoid(torch.randn(b, n, C.NV, generator=g)).to(torch.bfloat16)
+    return q, k, v, gg, beta
+
+
+@pytest.mark.parametrize("b", BATCHES)
+@pytest.mark.parametrize("n", [32, 64])
+@pytest.mark.parametrize("gdn_layer", [0, 5, 17])
+def test_gdn_scan_matches_the_oracle(pool_fixture, b: int, n: int, gdn_layer: int) -> None:
+    """Each row from its own prefix state read in place (layer 5's heads straddle pages). GDN_RTOL, GDN_ATOL (the
+    reference's: two bf16 steps at the largest outputs); with a stop at the last real token, the real positions are
+    bit for bit those without it and the padding positions zero."""
+    pool, slots, states = pool_fixture
+    ss = pass_slots(slots, b, seed=b * 7 + n + gdn_layer)
+    tables, _ = tables_for(pool, ss)
+    q, k, v, g, beta = gdn_inputs(b, n, seed=b + n + gdn_layer)
+    got = kernels.gdn_scan(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), pool, tables, gdn_layer)
+    s0 = torch.stack([states[s][1][gdn_layer] for s in ss])
+    want, _ = model_ref.gdn_scan(q.float(), k.float(), v.float(), g, beta.float(), s0)
+    torch.testing.assert_close(got.cpu().float(), want, rtol=GDN_RTOL, atol=GDN_ATOL)
+    rng = random.Random(b * n)
+    last = torch.tensor([n - 1 if r == 0 else rng.randrange(n) for r in range(b)], dtype=torch.int32)
+    stopped = kernels.gdn_scan(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), pool, tables, gdn_layer,
+                               last=last.cuda()).cpu()
+    for r in range(b):
+        end = int(last[r]) + 1
+        assert torch.equal(stopped[r, :end], got[r, :end].cpu())
+        assert not stopped[r, end:].any()
+
+
+def test_gdn_scan_writes_the_final_state_into_the_output_pages(pool_fixture) -> None:
+    pool, slots, states = pool_fixture
+    b, n = 3, 64
+    ss = [slots[33], 0, slots[100]]
+    tables, _ = tables_for(pool, ss)
+    q, k, v, g, beta = gdn_inputs(b, n, seed=42)
+    fresh = [pool.reserve(2, f"out {i}", 40) for i in range(b)]
+    out_tables = pool.tables.index_select(0, torch.tensor(fresh, device="cuda")).contiguous()
+    kernels.gdn_scan(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), pool, tables, 7, out_tables=out_tables)
+    torch.cuda.synchronize()
+    s0 = torch.stack([states[s][1][7] for s in ss])
+    _, s_fin = model_ref.gdn_scan(q.float(), k.float(), v.float(), g, beta.float(), s0)
+    for i, slot in enumerate(fresh):
+        got = pool.gather(slot)[1][7].cpu()
+        torch.testing.assert_close(got, s_fin[i], rtol=1e-4, atol=1e-5)
+        pool.release(slot)
+
+
+# ---------------------------------------------------------------- attention
+
+
+@pytest.mark.parametrize("b", BATCHES)
+@pytest.mark.parametrize("n", [32, 64])
+def test_attn_prep_rows_match_the_oracle(pool_fixture, b: int, n: int) -> None:
+    """Within two bf16 steps (the GPU's cos and sin may move a rounded value by one step); values bit for bit."""
+    pool, slots, _ = pool_fixture
+    ss = pass_slots(slots, b, seed=b + n)
+    _, pos = tables_for(pool, ss)
+    g = torch.Generator().manual_seed(b + n)
+    qn = 0.1 * torch.randn(C.HD, generator=g)
+    kn_w = 0.1 * torch.randn(C.HD, generator=g)
+    inv = model_ref.inv_freq()
+    pr = torch.randn(b * n, C.ATTN_PROJ, generator=g).to(torch.bfloat16)
+    kn = torch.empty(b * n, C.NKV, C.HD, dtype=torch.bfloat16, device="cuda")
+    vn = torch.empty_like(kn)
+    q = kernels.attn_prep_rows(pr.cuda(), (1 + qn).cuda(), (1 + kn_w).cuda(), inv.cuda(), pos, kn, vn, n).cpu()
+    for r in range(b):
+        rq, rk, rv, _ = model_ref.attn_prep(pr[r * n:(r + 1) * n], qn, kn_w, int(pos[r]))
+        sl = slice(r * n, (r + 1) * n)
+        torch.testing.assert_close(q[sl].float(), rq, rtol=2 * BF16_STEP, atol=2 * BF16_STEP)
+        torch.testing.assert_close(kn.cpu()[sl].float(), rk, rtol=2 * BF16_STEP, atol=2 * BF16_STEP)
+        assert torch.equal(vn.cpu()[sl].float(), rv)
+
+
+ATTN_RTOL, ATTN_ATOL = 2.0 ** -6, 2.0 ** -8
+
+
+@pytest.mark.parametrize("b", BATCHES)
+@pytest.mark.parametrize("n", [32, 64])
+def test_paged_attention_matches_the_oracle(pool_fixture, b: int, n: int) -> None:
+    """Prefix keys/values read in place (NaN past each prefix's end must not be read), then the new keys causally,
+    attention layers 0 and 5; ATTN_RTOL, ATTN_ATOL (the reference's: P is rounded to bf16 before P V)."""
+    pool, slots, states = pool_fixture
+    ss = pass_slots(slots, b, seed=b * 11 + n)
+    tables, pos = tables_for(pool, ss)
+    g = torch.Generator().manual_seed(b + n)
+    q = torch.randn(b * n, C.NQ, C.HD, generator=g).to(torch.bfloat16)
+    kn = torch.randn(b * n, C.NKV, C.HD, generator=g).to(torch.bfloat16)
+    vn = torch.randn(b * n, C.NKV, C.HD, generator=g).to(torch.bfloat16)
+    for layer in (0, 5):
+        got = kernels.paged_attention(q.cuda(), pool, tables, layer, pos, kn.cuda(), vn.cuda(), n).cpu()
+        assert not got.isnan().any(), "the kernel read a NaN past a prefix's last token"
+        for r in range(b):
+            kv = states[ss[r]][2][layer]
+            sl = slice(r * n, (r + 1) * n)
+            want = model_ref.attention(q[sl], kv[0], kv[1], kn[sl], vn[sl])
+            torch.testing.assert_close(got[sl].float(), want, rtol=ATTN_RTOL, atol=ATTN_ATOL)
