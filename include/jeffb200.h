@@ -36,9 +36,15 @@ int jb_device_status(int* status, int reset, void* stream);
 
 /* ---------------------------------------------------------------- int4 W4A16 + multi-LoRA products (S1) */
 
-/* Dequantise a packed group (for verification): words int32 (k/8, columns), scales and zeros (nullable) bf16
- * (k/group, columns) -> out bf16 (columns, k), bf16(fp32(u - z) * fp32(s)) with z = 8 when zeros is NULL.
- * Replaces int4.dequantize / unpack_kernel (int4.py:203-208, :258-262). */
+/* The reference's kernel word layout (int32 (k/8, columns); input 8i + j of column c in bits 4j..4j+3 of word
+ * (i, c), stored unsigned; int4.py:215-255) -> this library's kernel layout: the same words with the nibbles of
+ * inputs 0,2,4,6,1,3,5,7 in slots 0..7 (two neighbouring inputs per shift and mask). In place allowed. Load time.
+ * Replaces int4.pack_kernel's output as the kernels' input (int4.py:233-255). */
+int jb_int4_repack(const int32_t* words, int32_t* out, int k, int columns, void* stream);
+
+/* Dequantise a packed group (for verification): words int32 (k/8, columns) in the kernel layout, scales and zeros
+ * (nullable) bf16 (k/group, columns) -> out bf16 (columns, k), bf16(fp32(u - z) * fp32(s)) with z = 8 when zeros is
+ * NULL. Replaces int4.dequantize / unpack_kernel (int4.py:203-208, :258-262). */
 int jb_int4_dequant(const int32_t* words, const uint16_t* scales, const uint16_t* zeros, int k, int columns,
                     int group, uint16_t* out, void* stream);
 
@@ -48,9 +54,9 @@ int jb_int4_dequant(const int32_t* words, const uint16_t* scales, const uint16_t
 int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* lora_a, int rank, int pool_rows,
                    const int32_t* adapters, int row_len, uint16_t* mid, void* stream);
 
-/* The fused product: y (m, out) bf16 = bf16(x . W^T + mid . B[a]^T), W = dequantised int4 (words, scales, zeros as
- * jb_int4_dequant), the base product accumulated in fp32 by tcgen05 tensor cores from TMA-staged packed weights
- * dequantised in shared memory, then the LoRA expand (mid from jb_lora_shrink, B from lora_b (pool_rows, columns,
+/* The fused product: y (m, out) bf16 = bf16(x . W^T + mid . B[a]^T), W = dequantised int4 (kernel-layout words,
+ * scales, zeros as jb_int4_dequant), the base product accumulated in fp32 by tcgen05 tensor cores from TMA-staged
+ * packed weights dequantised in shared memory, then the LoRA expand (mid from jb_lora_shrink, B from lora_b (pool_rows, columns,
  * rank)) added into the same accumulator, rounded once. rank 0 (or mid NULL) leaves out the LoRA term.
  * Requires k % 64 == 0, columns % 64 == 0, out <= columns, ldy % 8 == 0, row_len % 32 == 0 and row_len % 128 == 0
  * or 128 % row_len == 0. Replaces int4_kernels.int4_product (int4_kernels.py:132-177) and Lin.__call__

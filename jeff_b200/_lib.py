@@ -76,8 +76,17 @@ def stream_ptr(stream: torch.cuda.Stream | None = None) -> int:
     return s.cuda_stream
 
 
+# Kernel launches each entry point makes (the product with LoRA makes two: shrink, then the fused GEMM); counted
+# by `call` so a caller can report how many of this library's kernels a recorded pass launches.
+_NO_LAUNCH = {"jb_abi_version", "jb_last_error", "jb_device_status"}
+launches = 0
+
+
 def call(name: str, *args) -> None:
+    global launches
     lib = load()
+    if name not in _NO_LAUNCH:
+        launches += 2 if (name == "jb_int4_lora_product" and args[11]) else 1
     status = getattr(lib, name)(*args)
     if status != 0:
         msg = lib.jb_last_error().decode(errors="replace")

@@ -24,6 +24,7 @@ from typing import Any
 import numpy as np
 import torch
 
+from jeff_b200 import _lib
 from jeff_b200 import constants as C
 from jeff_b200 import kernels
 from jeff_b200.fast_path import FastPath
@@ -104,6 +105,7 @@ class BatchedPath:
         self.prefix_inp_host = torch.zeros(psize, dtype=torch.int32).pin_memory()
         self.prefix_inp_np = self.prefix_inp_host.numpy()
         self.graphs: dict[tuple[int, int], tuple[torch.cuda.CUDAGraph, torch.Tensor]] = {}
+        self.graph_launches: dict[tuple[int, int], int] = {}   # this library's kernels in each decision graph
         self.prefix_graphs: dict[tuple[int, int], torch.cuda.CUDAGraph] = {}
         self.graph_pool = torch.cuda.graph_pool_handle()
         self.stream = torch.cuda.Stream(device=dev)
@@ -131,14 +133,20 @@ class BatchedPath:
 
     def _layers(self, x: torch.Tensor, adapters: torch.Tensor, n: int, t: int, gdn_tables: torch.Tensor,
                 attn_tables: torch.Tensor, pos: torch.Tensor, last: torch.Tensor | None,
-                real: torch.Tensor | None = None, out_tables: torch.Tensor | None = None) -> torch.Tensor | None:
-        """The decoder layers over t tokens (rows of n), in place on the residual x; returns the last d."""
+                real: torch.Tensor | None = None, out_tables: torch.Tensor | None = None,
+                trace: list[torch.Tensor] | None = None, first: int = 0,
+                stop: int | None = None) -> torch.Tensor | None:
+        """Decoder layers first..stop-1 (all by default) over t tokens (rows of n), in place on the residual x;
+        returns the last d. `trace` (eager runs only) receives each layer's residual stream bf16(x + d)."""
         f, ws, pool = self.fast, self.ws, self.pool
         b = t // n
         d: torch.Tensor | None = None
-        gi = ai = 0
+        gi = sum(1 for k in f.kinds[:first] if k == "linear_attention")
+        ai = first - gi
         prefix = out_tables is not None
-        for li, layer in enumerate(f.layers):
+        stop = len(f.layers) if stop is None else stop
+        for li in range(first, stop):
+            layer = f.layers[li]
             _, h = kernels.add_rms(x, d, layer["norm_in"], xo=x, h=ws.h[:t])
             proj = layer["proj"]
             pr = proj(h, adapters, n, ws.mid, ws.pr[:t * proj.out].view(t, proj.out))
@@ -171,9 +179,11 @@ class BatchedPath:
             gu = layer["mlp_in"](h, adapters, n, ws.mid, ws.gu[:t])
             act = kernels.silu_mul(gu, out=ws.act[:t])
             d = layer["mlp_down"](act, adapters, n, ws.mid, ws.d[:t])
+            if trace is not None:
+                trace.append((x.float() + d.float()).to(DT))
         return d
 
-    def body(self, b: int, n: int) -> torch.Tensor:
+    def body(self, b: int, n: int, trace: list[torch.Tensor] | None = None) -> torch.Tensor:
         """The recorded decision pass: B rows of N tokens from the packed input; returns probabilities (B, 255)."""
         f, ws = self.fast, self.ws
         v = self.views(b, n)
@@ -181,7 +191,7 @@ class BatchedPath:
         tables = ws.tables[:b]
         torch.index_select(self.pool.tables, 0, v["slots"], out=tables)
         x = kernels.embed(f.embed, v["ids"], out=ws.x[:t])
-        d = self._layers(x, v["adapters"], n, t, tables, tables, v["pos"], v["last"])
+        d = self._layers(x, v["adapters"], n, t, tables, tables, v["pos"], v["last"], trace=trace)
         assert d is not None
         hidden = kernels.rms_last(x, d, v["last"], n, f.final_w1, out=ws.hidden[:b])
         return kernels.readout_rows(hidden, f.readout_pool, f.temp_pool, v["adapters"], v["counts"],
@@ -208,8 +218,10 @@ class BatchedPath:
                 work()
         self.stream.synchronize()
         graph = torch.cuda.CUDAGraph()
+        before = _lib.launches
         with torch.cuda.graph(graph, pool=self.graph_pool, stream=self.stream):
             out = work()
+        self.last_capture_launches = _lib.launches - before
         torch.cuda.current_stream(self.device).wait_stream(self.stream)
         return graph, out
 
@@ -227,6 +239,7 @@ class BatchedPath:
                 raise ValueError(f"A pass of {b} x {n} tokens exceeds this path's workspace ({self.max_tokens})")
             self._pad_decision(b, n)
             self.graphs[(b, n)] = self._capture(lambda: self.body(b, n))
+            self.graph_launches[(b, n)] = self.last_capture_launches
         return self.graphs[(b, n)]
 
     def _pad_prefix(self, b: int, nb: int) -> None:
@@ -252,6 +265,35 @@ class BatchedPath:
             self.graph(b, n)
         torch.cuda.synchronize(self.device)
         return time.perf_counter() - started
+
+    def trace_pass(self, b: int, n: int, part: Sequence[tuple[int, int, Row]],
+                   lengths: Sequence[int]) -> tuple[torch.Tensor, list[torch.Tensor]]:
+        """One pass run eagerly (no graph) with each layer's residual stream kept: (probs (B, 255), per layer
+        (B * N, 1024) bf16). For parity tests."""
+        size = self.fill(b, n, part, lengths)
+        self.inp[:size].copy_(self.inp_host[:size])
+        trace: list[torch.Tensor] = []
+        probs = self.body(b, n, trace=trace).clone()
+        torch.cuda.synchronize(self.device)
+        return probs, trace
+
+    def layer_pass(self, li: int, x_in: torch.Tensor, b: int, n: int, part: Sequence[tuple[int, int, Row]],
+                   lengths: Sequence[int]) -> torch.Tensor:
+        """Decoder layer `li` alone, eagerly, on the residual stream x_in (B * N, 1024) bf16 of the staged rows:
+        returns its output residual stream bf16(x + d). For layer-local parity tests."""
+        size = self.fill(b, n, part, lengths)
+        self.inp[:size].copy_(self.inp_host[:size])
+        v = self.views(b, n)
+        t = b * n
+        tables = self.ws.tables[:b]
+        torch.index_select(self.pool.tables, 0, v["slots"], out=tables)
+        x = self.ws.x[:t]
+        x.copy_(x_in)
+        d = self._layers(x, v["adapters"], n, t, tables, tables, v["pos"], v["last"], first=li, stop=li + 1)
+        assert d is not None
+        out = (x.float() + d.float()).to(DT)
+        torch.cuda.synchronize(self.device)
+        return out
 
     # ------------------------------------------------------------ requests
 

@@ -1,31 +1,37 @@
 // S1: the int4 W4A16 product fused with the per-row multi-LoRA update, tcgen05 + TMA (sm_100a).
 //
-// y (M, out) = bf16( x (M, K) . W^T + mid . B[a]^T ), W = bf16(fp32(u - z) * fp32(s)) from the reference's int4
-// kernel layout (words (K/8, columns) int32, scales/zeros (K/G, columns) bf16).
+// y (M, out) = bf16( x (M, K) . W^T + mid . B[a]^T ), W = bf16(fp32(u - z) * fp32(s)) from int4 words in the kernel
+// layout (jb_int4_repack of the reference's layout: within each word the nibbles of inputs 0,2,4,6,1,3,5,7, so one
+// shift and one mask give two neighbouring inputs), scales/zeros (K/G, columns) bf16.
 //
-// One CTA computes a 128 x BN tile with 6 warps:
-//   warp 0      TMA producer: per 64-wide K block, the x tile (128 x 64 bf16, 128B swizzle), the packed words
-//               (8 x BN int32) and the group's scale (and zero) rows, into a STAGES-deep ring (mbarrier full[s]);
-//   warp 1      allocates BN TMEM columns; one thread issues tcgen05.mma (M=128, N=BN, K=16) x 4 per K block into
-//               the fp32 accumulator in TMEM and commits each stage back to the producer (empty[s]);
-//   warps 2-5   dequantise each stage's words into bf16 in the UMMA 128B-swizzled K-major layout (deq[s]), then run
-//               the epilogue: the LoRA expand operands (mid rows placed in their adapter's rank block, and the
-//               adapters' B rows) written over the now idle x / weight stages, 1-12 more MMAs into the same
-//               accumulator, TMEM -> registers -> bf16 -> swizzled smem -> TMA store (clipped to M x out).
+// One CTA computes a 256 x 128 tile (two 128-row halves sharing every dequantised weight tile) with 10 warps:
+//   warp 0      TMA producer: per 64-wide K block the x tile (256 x 64 bf16, 128B swizzle), the packed words
+//               (8 x 128 int32) and the group's scale (and zero) row, into a STAGES-deep ring (mbarrier full[s]);
+//   warp 1      allocates 256 TMEM columns; one thread issues tcgen05.mma (M=128, N=128, K=16) 4 x 2 per K block
+//               into the two fp32 accumulators and commits each stage back to the producer (empty[s]);
+//   warps 2-9   dequantise each stage's words (thread: one column, four words) into bf16 in the UMMA 128B-swizzled
+//               K-major layout (deq[s]); then the epilogue: the LoRA expand operands (each half's mid rows placed in
+//               their adapter's rank block, and the adapters' B rows) written over the idle rings, 1-12 more MMAs
+//               per half into the same accumulators, TMEM -> registers -> bf16 -> swizzled smem -> TMA store
+//               (clipped to M x out).
 // The base product is summed in fp32 in K order; the LoRA term joins the same fp32 accumulator; one rounding at the
 // end: the reference's cut-product rule (int4_kernels.py:1-30). No atomics: the result is deterministic.
 //
-// Dequantisation: nibble pairs become bf16 (128 + u) by OR-ing the exponent bits 0x4300, minus (128 + z) is the
+// Dequantisation: a nibble pair becomes bf16 (128 + u) by OR-ing the exponent bits 0x4300, minus (128 + z) is the
 // exact small integer u - z, times the scale in one bf16 multiply (a single rounding of an exact product), which is
 // bf16(fp32(u - z) * fp32(s)) bit for bit.
 
 namespace jb {
 namespace w4 {
 
-constexpr int BM = 128;
+constexpr int BM = 256;             // rows per CTA (two UMMA halves of 128)
+constexpr int HM = 128;             // rows per half
+constexpr int BN = 128;
 constexpr int BK = 64;
-constexpr int THREADS = 192;
-constexpr int MAX_EXPAND = 192;   // nA * rank columns of the expand operand (<= 3 swizzle atoms of 64)
+constexpr int STAGES = 4;
+constexpr int DEQ_WARPS = 8;
+constexpr int THREADS = 64 + DEQ_WARPS * 32;
+constexpr int MAX_EXPAND = 192;     // adapters per half x rank: columns of the expand operand (<= 3 swizzle atoms)
 
 struct Params {
   int M, K, columns, out, group;
@@ -36,11 +42,10 @@ struct Params {
   int* err;
 };
 
-template <int BN, int STAGES>
 struct Layout {
-  static constexpr int X_BYTES = BM * BK * 2;
-  static constexpr int W_BYTES = BN * BK * 2;
-  static constexpr int RAW_BYTES = 8 * BN * 4;
+  static constexpr int X_BYTES = BM * BK * 2;      // 32 KB: two 128-row swizzled tiles back to back
+  static constexpr int W_BYTES = BN * BK * 2;      // 16 KB
+  static constexpr int RAW_BYTES = 8 * BN * 4;     // 4 KB
   static constexpr int SC_BYTES = BN * 2;
   static constexpr int OFF_X = 0;
   static constexpr int OFF_W = OFF_X + STAGES * X_BYTES;
@@ -51,24 +56,22 @@ struct Layout {
   static constexpr int NBAR = 3 * STAGES + 3;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
-  static constexpr int ALLOC = BYTES + 1024;   // room to align the base to 1024 B
-  static_assert(STAGES * X_BYTES >= 3 * 16384 && STAGES * X_BYTES >= BM * BN * 2, "x ring too small to alias");
-  static_assert(STAGES * W_BYTES >= 3 * BN * 128, "weight ring too small to alias");
+  static constexpr int ALLOC = BYTES + 1024;       // room to align the base to 1024 B
+  static constexpr int SCRATCH = STAGES * (X_BYTES + W_BYTES);   // x and weight rings, contiguous, reused
+  static_assert(SCRATCH >= 4 * 3 * 16384, "rings too small for the LoRA expand operands");
+  static_assert(SCRATCH >= BM * BN * 2, "rings too small for the output staging");
+  static_assert(ALLOC <= 227 * 1024, "shared memory");
 };
 
-__device__ __forceinline__ uint32_t pair_bits(uint32_t w, int pair) {
-  // nibbles 2p and 2p+1 of w into the low bits of the two bf16 halves
-  uint32_t lo = (w >> (8 * pair)) & 0xFu;
-  uint32_t hi = (w >> (8 * pair + 4)) & 0xFu;
-  return lo | (hi << 16) | 0x43004300u;
-}
+// words in the kernel layout: nibble slot (j >> 1) + 4 (j & 1) holds input j of the word's eight
+__host__ __device__ constexpr int kernel_slot(int j) { return (j >> 1) + 4 * (j & 1); }
 
-// 8 weights of one word: bf16((u - z) * s) for u the 8 nibbles (input order), s2 = {s, s}, zb2 = {128 + z, 128 + z}
+// 8 weights of one kernel-layout word: bf16((u - z) * s) in input order, s2 = {s, s}, zb2 = {128 + z, 128 + z}
 __device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bfloat162 zb2) {
   uint32_t r[4];
 #pragma unroll
   for (int p = 0; p < 4; ++p) {
-    uint32_t t = pair_bits(w, p);
+    uint32_t t = ((w >> (4 * p)) & 0x000F000Fu) | 0x43004300u;   // inputs 2p, 2p + 1
     __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&t);
     v = __hmul2(__hsub2(v, zb2), s2);
     r[p] = *reinterpret_cast<uint32_t*>(&v);
@@ -81,12 +84,12 @@ __device__ __forceinline__ __nv_bfloat162 zero_pair(const __nv_bfloat16* zr, int
   return __floats2bfloat162_rn(128.0f + z, 128.0f + z);
 }
 
-template <int BN, int STAGES, bool ZERO>
+template <bool ZERO>
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_lora_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                       const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
                       const __grid_constant__ CUtensorMap tm_y, Params p) {
-  using L = Layout<BN, STAGES>;
+  using L = Layout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
@@ -106,13 +109,16 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int n0 = blockIdx.y * BN;
   const int nkb = p.K / BK;
   const bool has_lora = p.mid != nullptr && p.rank > 0;
-  const int n_adp = p.row_len >= BM ? 1 : BM / p.row_len;
-  const int ke = has_lora ? n_adp * p.rank : 0;   // expand K (multiple of 16)
+  const int n_adp = p.row_len >= HM ? 1 : HM / p.row_len;   // adapters per 128-row half
+  const int ke = has_lora ? n_adp * p.rank : 0;              // expand K (multiple of 16)
+  const int ke_pad = (ke + 63) & ~63;
+  const int atom_bytes_a = (ke_pad / 64) * HM * 128;         // one half's expand A operand
+  const int atom_bytes_b = (ke_pad / 64) * BN * 128;         // one half's expand B operand
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&deq[s], 4);
+      mbar_init(&deq[s], DEQ_WARPS);
       mbar_init(&empty[s], 1);
     }
     mbar_init(main_done, 1);
@@ -130,7 +136,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tmap(&tm_y);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, BN);
+    tmem_alloc(tmem_slot, 2 * BN);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -153,7 +159,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
   } else if (warp == 1) {
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(BM, BN);
+      constexpr uint32_t idesc = idesc_bf16(HM, BN);
       bool ok = true;
       for (int kb = 0; kb < nkb && ok; ++kb) {
         const int s = kb % STAGES;
@@ -161,27 +167,37 @@ __global__ void __launch_bounds__(THREADS, 1)
         ok = mbar_wait(&full[s], ph, abort_flag, p.err, 2) && mbar_wait(&deq[s], ph, abort_flag, p.err, 3);
         if (!ok) break;
         tc_fence_after();
-        const uint64_t ad = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES));
+        const uint64_t a0 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES));
+        const uint64_t a1 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES + HM * 128));
         const uint64_t bd = sw128_desc(smem_u32(smem + L::OFF_W + s * L::W_BYTES));
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) tc_mma_bf16(tmem, ad + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+        for (int kk = 0; kk < BK / 16; ++kk) {
+          tc_mma_bf16(tmem, a0 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+          tc_mma_bf16(tmem + BN, a1 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+        }
         tc_commit(&empty[s]);
       }
       tc_commit(main_done);
       if (ok && mbar_wait(lora_ready, 0, abort_flag, p.err, 4)) {
         tc_fence_after();
-        for (int j = 0; j < ke / 16; ++j) {
-          const int atom = j >> 2, w16 = j & 3;
-          const uint64_t ad = sw128_desc(smem_u32(smem + L::OFF_X + atom * 16384)) + 2 * w16;
-          const uint64_t bd = sw128_desc(smem_u32(smem + L::OFF_W + atom * BN * 128)) + 2 * w16;
-          tc_mma_bf16(tmem, ad, bd, idesc, 1);
+        for (int h = 0; h < 2; ++h) {
+          uint8_t* mid_t = smem + L::OFF_X + h * atom_bytes_a;
+          uint8_t* b_t = smem + L::OFF_X + 2 * atom_bytes_a + h * atom_bytes_b;
+          for (int j = 0; j < ke / 16; ++j) {
+            const int atom = j >> 2, w16 = j & 3;
+            const uint64_t ad = sw128_desc(smem_u32(mid_t + atom * HM * 128)) + 2 * w16;
+            const uint64_t bd = sw128_desc(smem_u32(b_t + atom * BN * 128)) + 2 * w16;
+            tc_mma_bf16(tmem + h * BN, ad, bd, idesc, 1);
+          }
         }
       }
       tc_commit(acc_full);
     }
   } else {
-    // ---------------- dequantisers, then the epilogue: 128 threads
+    // ---------------- dequantisers (thread: column n, words 4 wh .. 4 wh + 3), then the epilogue: 256 threads
     const int et = threadIdx.x - 64;
+    const int n = et & (BN - 1);
+    const int wh = et >> 7;
     for (int kb = 0; kb < nkb; ++kb) {
       const int s = kb % STAGES;
       const bool ok = mbar_wait(&full[s], (kb / STAGES) & 1, abort_flag, p.err, 5);
@@ -191,74 +207,74 @@ __global__ void __launch_bounds__(THREADS, 1)
       const __nv_bfloat16* zr = ZERO ? reinterpret_cast<const __nv_bfloat16*>(smem + L::OFF_ZR + s * L::SC_BYTES)
                                      : nullptr;
       uint8_t* wt = smem + L::OFF_W + s * L::W_BYTES;
+      const __nv_bfloat162 s2 = __bfloat162bfloat162(sc[n]);
+      const __nv_bfloat162 zb2 = zero_pair(zr, n);
+      uint32_t w[4];
 #pragma unroll
-      for (int nn = 0; nn < BN / 128; ++nn) {
-        const int n = et + nn * 128;
-        const __nv_bfloat162 s2 = __bfloat162bfloat162(sc[n]);
-        const __nv_bfloat162 zb2 = zero_pair(zr, n);
+      for (int r = 0; r < 4; ++r) w[r] = static_cast<uint32_t>(raw[(4 * wh + r) * BN + n]);
 #pragma unroll
-        for (int r = 0; r < 8; ++r) {
-          const uint4 v = dequant8(static_cast<uint32_t>(raw[r * BN + n]), s2, zb2);
-          *reinterpret_cast<uint4*>(wt + sw128_offset(n, r)) = v;
-        }
-      }
+      for (int r = 0; r < 4; ++r)
+        *reinterpret_cast<uint4*>(wt + sw128_offset(n, 4 * wh + r)) = dequant8(w[r], s2, zb2);
       fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) mbar_arrive(&deq[s]);
     }
 
-    // ---------------- epilogue
-    const int row = 32 * (warp & 3) + lane;   // the TMEM lane this thread may read
+    // ---------------- epilogue: thread = row (half h, TMEM lane quadrant of its warp)
+    const int h = (warp - 2) >> 2;
+    const int lrow = 32 * (warp & 3) + lane;       // row within the half = its TMEM lane
+    const int row = h * HM + lrow;
     if (et == 0) *epi_ok = mbar_wait(main_done, 0, abort_flag, p.err, 6) ? 1 : 0;
-    named_barrier(1, 128);
+    named_barrier(1, DEQ_WARPS * 32);
     const bool go = *epi_ok != 0;
     if (go && has_lora) {
-      // mid rows into their adapter block of the expand A operand (over the x ring; all x stages are consumed)
-      const int ke_pad = (ke + 63) & ~63;
+      // this half's mid rows into their adapter block of its expand A operand (over the consumed rings)
       const int gm = m0 + row;
-      const int block_of_row = (p.row_len >= BM) ? 0 : (row / p.row_len);
-      uint8_t* mid_t = smem + L::OFF_X;
+      const int block_of_row = (p.row_len >= HM) ? 0 : (lrow / p.row_len);
+      uint8_t* mid_t = smem + L::OFF_X + h * atom_bytes_a;
       for (int c8 = 0; c8 < ke_pad / 8; ++c8) {
         const int col = c8 * 8;
         uint4 v = make_uint4(0, 0, 0, 0);
         if (col < ke && gm < p.M && col / p.rank == block_of_row)
           v = *reinterpret_cast<const uint4*>(p.mid + (size_t)gm * p.rank + (col % p.rank));
-        *reinterpret_cast<uint4*>(mid_t + (col >> 6) * 16384 + sw128_offset(row, (col & 63) >> 3)) = v;
+        *reinterpret_cast<uint4*>(mid_t + (col >> 6) * (HM * 128) + sw128_offset(lrow, (col & 63) >> 3)) = v;
       }
-      // the tile's adapters' B rows (over the weight ring)
-      uint8_t* b_t = smem + L::OFF_W;
-      const int first_row_block = m0 / p.row_len;
-      for (int nn = 0; nn < BN / 128; ++nn) {
-        const int n = et + nn * 128;
-        const int gn = n0 + n;
+      // the B rows of the half's adapters: thread et builds column et & 127 of half et >> 7
+      {
+        const int bh = et >> 7;
+        const int bn = et & (BN - 1);
+        const int gn = n0 + bn;
+        uint8_t* b_t = smem + L::OFF_X + 2 * atom_bytes_a + bh * atom_bytes_b;
+        const int first_row_block = (m0 + bh * HM) / p.row_len;
         for (int c8 = 0; c8 < ke_pad / 8; ++c8) {
           const int col = c8 * 8;
           uint4 v = make_uint4(0, 0, 0, 0);
           const int blk = col / p.rank;
-          if (col < ke && gn < p.columns && (first_row_block + blk) * p.row_len < p.M) {
-            int a = p.adapters[first_row_block + blk];
+          if (col < ke && gn < p.columns && (first_row_block + blk) * p.row_len < p.M &&
+              m0 + bh * HM < p.M) {
+            const int a = p.adapters[first_row_block + blk];
             if (a >= 0 && a < p.pool_rows)
               v = *reinterpret_cast<const uint4*>(p.lora_b + ((size_t)a * p.columns + gn) * p.rank + (col % p.rank));
           }
-          *reinterpret_cast<uint4*>(b_t + (col >> 6) * (BN * 128) + sw128_offset(n, (col & 63) >> 3)) = v;
+          *reinterpret_cast<uint4*>(b_t + (col >> 6) * (BN * 128) + sw128_offset(bn, (col & 63) >> 3)) = v;
         }
       }
       fence_proxy_async_smem();
     }
-    named_barrier(1, 128);
+    named_barrier(1, DEQ_WARPS * 32);
     if (et == 0) mbar_arrive(lora_ready);
     if (et == 0) *epi_ok = (go && mbar_wait(acc_full, 0, abort_flag, p.err, 7)) ? 1 : 0;
-    named_barrier(1, 128);
+    named_barrier(1, DEQ_WARPS * 32);
     if (*epi_ok) {
       tc_fence_after();
-      uint8_t* out_t = smem + L::OFF_X;
-      const uint32_t lane_addr = tmem + ((uint32_t)(32 * (warp & 3)) << 16);
+      uint8_t* out_t = smem + L::OFF_X + h * (HM * BN * 2);   // per half: two 128 x 64 swizzled tiles
+      const uint32_t lane_addr = tmem + h * BN + ((uint32_t)(32 * (warp & 3)) << 16);
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(lane_addr + c * 32, r);
         tc_wait_ld();
-        const int half = (c * 32) >> 6;
+        const int half64 = (c * 32) >> 6;
         const int chunk0 = ((c * 32) & 63) >> 3;
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
@@ -267,14 +283,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           v.y = pack_bf2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
           v.z = pack_bf2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
           v.w = pack_bf2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
-          *reinterpret_cast<uint4*>(out_t + half * 16384 + sw128_offset(row, chunk0 + q)) = v;
+          *reinterpret_cast<uint4*>(out_t + half64 * 16384 + sw128_offset(lrow, chunk0 + q)) = v;
         }
       }
       fence_proxy_async_smem();
-      named_barrier(1, 128);
+      named_barrier(1, DEQ_WARPS * 32);
       if (et == 0) {
-        for (int h = 0; h < BN / 64; ++h)
-          if (n0 + h * 64 < p.out) tma_store_2d(&tm_y, out_t + h * 16384, n0 + h * 64, m0);
+        for (int hh = 0; hh < 2; ++hh) {
+          if (m0 + hh * HM >= p.M) continue;
+          for (int c = 0; c < BN / 64; ++c)
+            if (n0 + c * 64 < p.out)
+              tma_store_2d(&tm_y, smem + L::OFF_X + hh * (HM * BN * 2) + c * 16384, n0 + c * 64, m0 + hh * HM);
+        }
         tma_store_commit_and_wait();
       }
     }
@@ -284,11 +304,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, BN);
+    tmem_dealloc(tmem, 2 * BN);
   }
 }
 
 // ------------------------------------------------------------------ LoRA first factor (mma.sync, small)
+//
+// mid (M, R) = bf16(x A[a]^T): one CTA of 4 warps per 16 rows; warp w sums inputs [w K / 4, (w + 1) K / 4) with
+// bf16 mma.sync in fp32, four k-steps in flight; the four partial sums are added in warp order through shared
+// memory (a fixed order: deterministic), rounded once.
 
 template <int NB>   // rank / 8 output blocks
 __global__ void __launch_bounds__(128) lora_shrink_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
@@ -296,9 +320,9 @@ __global__ void __launch_bounds__(128) lora_shrink_kernel(const __nv_bfloat16* _
                                                           const int* __restrict__ adapters, int row_len,
                                                           __nv_bfloat16* __restrict__ mid) {
   constexpr int R = NB * 8;
+  __shared__ float part[4][16][R + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = (blockIdx.x * 4 + warp) * 16;
-  if (m0 >= M) return;
+  const int m0 = blockIdx.x * 16;
   int a = adapters[m0 / row_len];
   if (a < 0 || a >= pool_rows) a = 0;
   const __nv_bfloat16* Aa = A + (size_t)a * R * K;
@@ -308,7 +332,10 @@ __global__ void __launch_bounds__(128) lora_shrink_kernel(const __nv_bfloat16* _
   for (int i = 0; i < NB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
   const __nv_bfloat16* x0 = x + (size_t)(m0 + g) * K;
   const __nv_bfloat16* x1 = x0 + (size_t)8 * K;
-  for (int k0 = 0; k0 < K; k0 += 16) {
+  const int kspan = K / 4;
+  const int kbeg = warp * kspan, kend = kbeg + kspan;
+#pragma unroll 4
+  for (int k0 = kbeg; k0 < kend; k0 += 16) {
     const uint32_t a0 = *reinterpret_cast<const uint32_t*>(x0 + k0 + 2 * t);
     const uint32_t a1 = *reinterpret_cast<const uint32_t*>(x1 + k0 + 2 * t);
     const uint32_t a2 = *reinterpret_cast<const uint32_t*>(x0 + k0 + 8 + 2 * t);
@@ -328,8 +355,16 @@ __global__ void __launch_bounds__(128) lora_shrink_kernel(const __nv_bfloat16* _
 #pragma unroll
   for (int nb = 0; nb < NB; ++nb) {
     const int col = nb * 8 + 2 * t;
-    *reinterpret_cast<uint32_t*>(mid + (size_t)(m0 + g) * R + col) = pack_bf2(acc[nb][0], acc[nb][1]);
-    *reinterpret_cast<uint32_t*>(mid + (size_t)(m0 + g + 8) * R + col) = pack_bf2(acc[nb][2], acc[nb][3]);
+    part[warp][g][col] = acc[nb][0];
+    part[warp][g][col + 1] = acc[nb][1];
+    part[warp][g + 8][col] = acc[nb][2];
+    part[warp][g + 8][col + 1] = acc[nb][3];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < 16 * R; i += 128) {
+    const int r = i / R, c = i % R;
+    const float v = ((part[0][r][c] + part[1][r][c]) + part[2][r][c]) + part[3][r][c];
+    mid[(size_t)(m0 + r) * R + c] = __float2bfloat16_rn(v);
   }
 }
 
@@ -349,22 +384,32 @@ __global__ void int4_dequant_kernel(const int32_t* __restrict__ words, const __n
   *reinterpret_cast<uint4*>(out + (size_t)c * K + 8 * i) = v;
 }
 
-template <int BN, int STAGES, bool ZERO>
+template <bool ZERO>
 int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz,
            const CUtensorMap& ty, const Params& p, cudaStream_t stream) {
-  using L = Layout<BN, STAGES>;
-  auto kernel = w4a16_lora_kernel<BN, STAGES, ZERO>;
-  static bool configured[8] = {};
+  auto kernel = w4a16_lora_kernel<ZERO>;
+  static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 8 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::ALLOC);
+  if (dev < 64 && !configured[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout::ALLOC);
     if (e != cudaSuccess) return status_of(e, "w4a16: cudaFuncSetAttribute");
     configured[dev] = true;
   }
   dim3 grid((p.M + BM - 1) / BM, (p.columns + BN - 1) / BN);
-  kernel<<<grid, THREADS, L::ALLOC, stream>>>(tx, tw, ts, tz, ty, p);
+  kernel<<<grid, THREADS, Layout::ALLOC, stream>>>(tx, tw, ts, tz, ty, p);
   return check_launch("w4a16_lora_kernel");
+}
+
+// reference word layout (input 8i + j in bits 4j) -> kernel layout (input j in slot kernel_slot(j)); in place ok
+__global__ void int4_repack_kernel(const int32_t* __restrict__ in, int32_t* __restrict__ out, size_t n) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const uint32_t w = static_cast<uint32_t>(in[i]);
+  uint32_t r = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) r |= ((w >> (4 * j)) & 0xFu) << (4 * kernel_slot(j));
+  out[i] = static_cast<int32_t>(r);
 }
 
 }  // namespace w4
@@ -390,10 +435,10 @@ extern "C" int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* l
                               const int32_t* adapters, int row_len, uint16_t* mid, void* stream) {
   JB_REQUIRE(x && lora_a && adapters && mid, "jb_lora_shrink: null pointer");
   JB_REQUIRE(m > 0 && m % 16 == 0, "jb_lora_shrink: m %d must be a positive multiple of 16", m);
-  JB_REQUIRE(k > 0 && k % 16 == 0, "jb_lora_shrink: k %d must be a positive multiple of 16", k);
+  JB_REQUIRE(k > 0 && k % 64 == 0, "jb_lora_shrink: k %d must be a positive multiple of 64", k);
   JB_REQUIRE(row_len > 0 && row_len % 16 == 0, "jb_lora_shrink: row_len %d must be a multiple of 16", row_len);
   JB_REQUIRE(pool_rows > 0, "jb_lora_shrink: pool_rows %d", pool_rows);
-  dim3 grid((m / 16 + 3) / 4);
+  dim3 grid(m / 16);
   auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
   auto ab = reinterpret_cast<const __nv_bfloat16*>(lora_a);
   auto mb = reinterpret_cast<__nv_bfloat16*>(mid);
@@ -425,16 +470,16 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
   if (lora) {
     JB_REQUIRE(lora_b && adapters, "jb_w4a16_lora: LoRA needs lora_b and adapters");
     JB_REQUIRE(rank % 16 == 0 && rank <= 64, "jb_w4a16_lora: rank %d (16, 32, 48 or 64)", rank);
-    JB_REQUIRE(row_len > 0 && row_len % 32 == 0 && (row_len % w4::BM == 0 || w4::BM % row_len == 0),
+    JB_REQUIRE(row_len > 0 && row_len % 32 == 0 && (row_len % w4::HM == 0 || w4::HM % row_len == 0),
                "jb_w4a16_lora: row_len %d must be a multiple of 32 that divides or is divided by 128", row_len);
-    const int n_adp = row_len >= w4::BM ? 1 : w4::BM / row_len;
+    const int n_adp = row_len >= w4::HM ? 1 : w4::HM / row_len;
     JB_REQUIRE(n_adp * rank <= w4::MAX_EXPAND, "jb_w4a16_lora: %d adapters per tile x rank %d exceeds %d", n_adp,
                rank, w4::MAX_EXPAND);
     JB_REQUIRE(pool_rows > 0, "jb_w4a16_lora: pool_rows %d", pool_rows);
   }
   CUtensorMap tx, tw, ts, tz, ty;
   int st;
-  constexpr int BN = 128;
+  constexpr int BN = w4::BN;
   if ((st = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, m, (uint64_t)k * 2, 64, w4::BM,
                          CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
@@ -452,15 +497,23 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
   } else {
     tz = ts;
   }
-  if ((st = make_tmap_2d(&ty, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, m, (uint64_t)ldy * 2, 64, w4::BM,
+  if ((st = make_tmap_2d(&ty, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, m, (uint64_t)ldy * 2, 64, w4::HM,
                          CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
   w4::Params p{m, k, columns, out, group,
                lora ? reinterpret_cast<const __nv_bfloat16*>(mid) : nullptr,
                reinterpret_cast<const __nv_bfloat16*>(lora_b), adapters, lora ? rank : 0, row_len > 0 ? row_len : 128,
                pool_rows, device_status_word()};
-  if (zeros) return w4::launch<BN, 5, true>(tx, tw, ts, tz, ty, p, (cudaStream_t)stream);
-  return w4::launch<BN, 5, false>(tx, tw, ts, tz, ty, p, (cudaStream_t)stream);
+  if (zeros) return w4::launch<true>(tx, tw, ts, tz, ty, p, (cudaStream_t)stream);
+  return w4::launch<false>(tx, tw, ts, tz, ty, p, (cudaStream_t)stream);
+}
+
+extern "C" int jb_int4_repack(const int32_t* words, int32_t* out, int k, int columns, void* stream) {
+  JB_REQUIRE(words && out, "jb_int4_repack: null pointer");
+  JB_REQUIRE(k > 0 && k % 8 == 0 && columns > 0, "jb_int4_repack: k %d, columns %d", k, columns);
+  const size_t n = (size_t)(k / 8) * columns;
+  w4::int4_repack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(words, out, n);
+  return check_launch("int4_repack_kernel");
 }
 
 extern "C" int jb_int4_lora_product(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,

@@ -32,7 +32,7 @@ class DeviceLin:
         self.out = grp.out
         self.group = p.group
         self.columns = p.columns
-        self.words = p.words.to(device)
+        self.words = kernels.int4_repack(p.words.to(device))     # the kernels' word layout
         self.scales = p.scales.to(device)
         self.zeros = p.zeros.to(device) if p.zeros is not None else None
         self.rank = grp.rank
@@ -157,3 +157,16 @@ class FastPath:
 
     def weight_bytes(self) -> int:
         return sum(lin.nbytes() for lin in self.lins)
+
+    def tensors(self) -> list[torch.Tensor]:
+        """Every device tensor of the weights and adapter pools, in a fixed order (the NCCL broadcast at load)."""
+        out = [self.embed, self.final_w1, self.readout_pool, self.temp_pool, self.inv_freq]
+        for layer in self.layers:
+            for key in sorted(layer):
+                value = layer[key]
+                if isinstance(value, torch.Tensor):
+                    out.append(value)
+                elif isinstance(value, DeviceLin):
+                    out += [t for t in (value.words, value.scales, value.zeros, value.lora_a, value.lora_b)
+                            if t is not None]
+        return out

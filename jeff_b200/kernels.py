@@ -41,8 +41,15 @@ def _pass_rows(t: int, n: int) -> int:
 # ---------------------------------------------------------------- int4 products
 
 
+def int4_repack(words: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The reference's kernel word layout -> this library's kernel layout (jb_int4_repack), on the device."""
+    out = out if out is not None else torch.empty_like(words)
+    _lib.call("jb_int4_repack", ptr(words), ptr(out), words.shape[0] * 8, words.shape[1], stream_ptr())
+    return out
+
+
 def int4_dequant(words: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor | None, group: int) -> torch.Tensor:
-    """The packed group dequantised on the device: (columns, k) bf16."""
+    """The packed group (kernel-layout words) dequantised on the device: (columns, k) bf16."""
     k, columns = words.shape[0] * 8, words.shape[1]
     out = torch.empty(columns, k, dtype=DT, device=words.device)
     _lib.call("jb_int4_dequant", ptr(words), ptr(scales), ptr(zeros), k, columns, group, ptr(out), stream_ptr())
@@ -64,7 +71,8 @@ def int4_product(x: torch.Tensor, words: torch.Tensor, scales: torch.Tensor, zer
                  adapters: torch.Tensor | None, row_len: int, mid: torch.Tensor | None = None,
                  y: torch.Tensor | None = None) -> torch.Tensor:
     """y (m, out) = bf16(x W^T + bf16(x A[a]^T) B[a]^T) for row a = adapters[t // row_len] of token t: the fused
-    product of one group (module docstring). lora_a (rows, R, k), lora_b (rows, columns, R) bf16, or None."""
+    product of one group (module docstring); `words` in the kernel layout (int4_repack). lora_a (rows, R, k),
+    lora_b (rows, columns, R) bf16, or None."""
     m, k = x.shape
     columns = words.shape[1]
     if words.shape[0] * 8 != k:

@@ -87,18 +87,33 @@ class ModelWeights:
     layers: list[LayerWeights] = field(default_factory=list)
 
 
-def _group(seed: int, prefix: str, names: list[str], sizes: list[int], k: int, fmt: str) -> FusedGroup:
+def _skeleton_pack(out: int, k: int, fmt: str) -> PackedInt4:
+    """Correctly shaped placeholders of a packed group (filled later, e.g. by a broadcast from another rank)."""
+    group = 64 if fmt == "g64" else 128
+    columns = -(-out // C.KERNEL_COLUMNS) * C.KERNEL_COLUMNS
+    zeros = None if fmt == "g64" else torch.zeros(k // group, columns, dtype=DT)
+    return PackedInt4(torch.zeros(k // C.WORD, columns, dtype=torch.int32), torch.zeros(k // group, columns, dtype=DT),
+                      zeros, group, out)
+
+
+def _group(seed: int, prefix: str, names: list[str], sizes: list[int], k: int, fmt: str,
+           skeleton: bool = False) -> FusedGroup:
+    adapted = [n.rsplit(".", 1)[-1] in C.LORA_TARGETS for n in names]
+    if skeleton:
+        return FusedGroup([prefix + n for n in names], sizes, k, _skeleton_pack(sum(sizes), k, fmt),
+                          torch.empty(0, dtype=DT), adapted, C.LORA_RANK * sum(adapted))
     ws = [normal(seed, prefix + n, (s, k), 0.02) for n, s in zip(names, sizes, strict=True)]
     packed, deq = quantize_pack(torch.cat(ws), fmt)
-    adapted = [n.rsplit(".", 1)[-1] in C.LORA_TARGETS for n in names]
     return FusedGroup([prefix + n for n in names], sizes, k, packed, deq, adapted, C.LORA_RANK * sum(adapted))
 
 
-def make_model(spec: ModelSpec) -> ModelWeights:
-    """The synthetic base of `spec` (module docstring). The layer kinds repeat (GDN, GDN, GDN, attention)."""
+def make_model(spec: ModelSpec, skeleton: bool = False) -> ModelWeights:
+    """The synthetic base of `spec` (module docstring). The layer kinds repeat (GDN, GDN, GDN, attention).
+    skeleton=True: the same shapes with placeholder values, for a replica whose weights arrive by broadcast."""
     s = spec.seed
     kinds = [C.LAYER_KINDS[i % 4] for i in range(spec.layers)]
-    embed = normal(s, "embed_tokens", (spec.vocab, C.HIDDEN), 0.02).to(DT)
+    embed = (torch.zeros(spec.vocab, C.HIDDEN, dtype=DT) if skeleton
+             else normal(s, "embed_tokens", (spec.vocab, C.HIDDEN), 0.02).to(DT))
 
     def norm(name: str, n: int) -> torch.Tensor:
         if spec.norm_noise:
@@ -109,16 +124,16 @@ def make_model(spec: ModelSpec) -> ModelWeights:
     for i, kind in enumerate(kinds):
         p = f"layers.{i}."
         groups = {
-            "mlp_in": _group(s, p, ["mlp.gate_proj", "mlp.up_proj"], [C.INTER, C.INTER], C.HIDDEN, spec.fmt),
-            "mlp_down": _group(s, p, ["mlp.down_proj"], [C.HIDDEN], C.INTER, spec.fmt),
+            "mlp_in": _group(s, p, ["mlp.gate_proj", "mlp.up_proj"], [C.INTER, C.INTER], C.HIDDEN, spec.fmt, skeleton),
+            "mlp_down": _group(s, p, ["mlp.down_proj"], [C.HIDDEN], C.INTER, spec.fmt, skeleton),
         }
         layer = LayerWeights(kind, norm(p + "input_layernorm", C.HIDDEN), norm(p + "post_attention_layernorm", C.HIDDEN),
                              groups)
         if kind == "linear_attention":
             la = "linear_attn."
             groups["proj"] = _group(s, p, [la + "in_proj_qkv", la + "in_proj_z", la + "in_proj_b", la + "in_proj_a"],
-                                    [C.QKV_DIM, C.Z_DIM, C.NV, C.NV], C.HIDDEN, spec.fmt)
-            groups["out"] = _group(s, p, [la + "out_proj"], [C.HIDDEN], C.NV * C.DV, spec.fmt)
+                                    [C.QKV_DIM, C.Z_DIM, C.NV, C.NV], C.HIDDEN, spec.fmt, skeleton)
+            groups["out"] = _group(s, p, [la + "out_proj"], [C.HIDDEN], C.NV * C.DV, spec.fmt, skeleton)
             layer.conv = uniform(s, p + la + "conv1d", (C.QKV_DIM, C.CONV), -0.5, 0.5).to(DT)
             layer.A_log = torch.log(uniform(s, p + la + "A_log", (C.NV,), 0.0, 16.0).clamp_min(1e-3))
             layer.dt_bias = torch.ones(C.NV) + (normal(s, p + la + "dt_bias", (C.NV,), spec.norm_noise)
@@ -128,8 +143,8 @@ def make_model(spec: ModelSpec) -> ModelWeights:
         else:
             sa = "self_attn."
             groups["proj"] = _group(s, p, [sa + "q_proj", sa + "k_proj", sa + "v_proj"],
-                                    [C.NQ * 2 * C.HD, C.NKV * C.HD, C.NKV * C.HD], C.HIDDEN, spec.fmt)
-            groups["out"] = _group(s, p, [sa + "o_proj"], [C.HIDDEN], C.NQ * C.HD, spec.fmt)
+                                    [C.NQ * 2 * C.HD, C.NKV * C.HD, C.NKV * C.HD], C.HIDDEN, spec.fmt, skeleton)
+            groups["out"] = _group(s, p, [sa + "o_proj"], [C.HIDDEN], C.NQ * C.HD, spec.fmt, skeleton)
             layer.q_norm = norm(p + sa + "q_norm", C.HD)
             layer.k_norm = norm(p + sa + "k_norm", C.HD)
         model.layers.append(layer)
@@ -148,9 +163,10 @@ class AdapterWeights:
     matrices: dict[str, tuple[torch.Tensor, torch.Tensor]] = field(default_factory=dict)  # per matrix (A, sB)
 
 
-def make_adapter(model: ModelWeights, index: int, seed: int, alpha: float = 32.0) -> AdapterWeights:
+def make_adapter(model: ModelWeights, index: int, seed: int, alpha: float = 32.0,
+                 skeleton: bool = False) -> AdapterWeights:
     """A rank-16 adapter of every LoRA target: A ~ N(0, 0.02), B ~ N(0, 0.01), scale alpha / 16; readout
-    N(0, 0.02); temperature U(0.5, 2)."""
+    N(0, 0.02); temperature U(0.5, 2). skeleton=True: zeros of the same shapes (filled by a broadcast)."""
     name = f"adapter-{index}"
     scale = alpha / C.LORA_RANK
     lora: dict[tuple[int, str], tuple[torch.Tensor, torch.Tensor]] = {}
@@ -163,7 +179,9 @@ def make_adapter(model: ModelWeights, index: int, seed: int, alpha: float = 32.0
             b_all = torch.zeros(grp.out, grp.rank, dtype=DT)
             r0 = o0 = 0
             for mname, size, adapted in zip(grp.names, grp.sizes, grp.adapted, strict=True):
-                if adapted:
+                if adapted and skeleton:
+                    r0 += C.LORA_RANK
+                elif adapted:
                     a = normal(seed, f"{name}/{mname}/A", (C.LORA_RANK, grp.k), 0.02).to(DT)
                     b = (normal(seed, f"{name}/{mname}/B", (size, C.LORA_RANK), 0.01) * scale).to(DT)
                     a_all[r0:r0 + C.LORA_RANK] = a
@@ -172,6 +190,8 @@ def make_adapter(model: ModelWeights, index: int, seed: int, alpha: float = 32.0
                     r0 += C.LORA_RANK
                 o0 += size
             lora[(i, key)] = (a_all, b_all)
+    if skeleton:
+        return AdapterWeights(name, lora, torch.zeros(C.READOUT_ROWS, C.HIDDEN, dtype=DT), 1.0, matrices)
     readout = normal(seed, f"{name}/readout", (C.READOUT_ROWS, C.HIDDEN), 0.02).to(DT)
     temperature = float(uniform(seed, f"{name}/temperature", (1,), 0.5, 2.0)[0])
     return AdapterWeights(name, lora, readout, temperature, matrices)

@@ -145,17 +145,23 @@ def attn_prep(pr: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor, pos0: int,
     return norm_rope(queries, q_w), norm_rope(keys, k_w), values, gate
 
 
-def attention(q: torch.Tensor, kp: torch.Tensor, vp: torch.Tensor, kn: torch.Tensor, vn: torch.Tensor) -> torch.Tensor:
+def attention(q: torch.Tensor, kp: torch.Tensor, vp: torch.Tensor, kn: torch.Tensor, vn: torch.Tensor,
+              round_weights: bool = False) -> torch.Tensor:
     """One row: q (N, 8, 256) over its prefix keys/values kp, vp (P, 2, 256) fully and its new kn, vn (N, 2, 256)
-    causally; query head h reads key/value head h // 4; float32 softmax. Returns (N, 8, 256) float32."""
+    causally; query head h reads key/value head h // 4; float32 softmax. round_weights: the unnormalised weights
+    exp(s - max) are rounded to bf16 before the value product and the sum taken from the unrounded ones, as the
+    reference's paged kernel does (batched_kernels.py:405-412). Returns (N, 8, 256) float32."""
     n, p = q.shape[0], kp.shape[0]
     keys = torch.cat([kp, kn]).float().repeat_interleave(NQ // NKV, 1)
     values = torch.cat([vp, vn]).float().repeat_interleave(NQ // NKV, 1)
     scores = torch.einsum("nhd,mhd->hnm", q.float(), keys) * HD ** -0.5
     m = torch.arange(p + n)
     allowed = (m[None, :] < p) | (m[None, :] - p <= torch.arange(n)[:, None])
-    weights = scores.masked_fill(~allowed, float("-inf")).softmax(-1)
-    return torch.einsum("hnm,mhd->nhd", weights, values)
+    scores = scores.masked_fill(~allowed, float("-inf"))
+    if not round_weights:
+        return torch.einsum("hnm,mhd->nhd", scores.softmax(-1), values)
+    e = torch.exp(scores - scores.amax(-1, keepdim=True))
+    return torch.einsum("hnm,mhd->nhd", bf(e), values) / e.sum(-1).transpose(0, 1)[..., None]
 
 
 def gate_mul(o: torch.Tensor, gate: torch.Tensor, exact: bool = False) -> torch.Tensor:
@@ -265,7 +271,7 @@ def run_pass(model, rows: list[RowIn], exact: bool = False, want_prefix: bool = 
                 q, kn, vn, gate = attn_prep(pr[starts[i]:starts[i] + n], layer.q_norm, layer.k_norm,
                                             row.prefix.length, exact)
                 kp, vp = row.prefix.keys[ai], row.prefix.values[ai]
-                o = r(attention(q, kp, vp, kn, vn))
+                o = r(attention(q, kp, vp, kn, vn, round_weights=not exact))
                 ys.append(gate_mul(o, gate, exact))
                 if outs is not None:
                     outs[i].keys.append(torch.cat([kp.float(), kn]))

@@ -85,12 +85,20 @@ def tables_for(pool: PrefixPool, slots: list[int]) -> tuple[torch.Tensor, torch.
 # ---------------------------------------------------------------- int4
 
 
+def test_int4_repack_permutes_nibbles() -> None:
+    """The kernel word layout: input j of each word in nibble slot (j >> 1) + 4 (j & 1)."""
+    words = torch.tensor([[0x76543210, -0x10000000]], dtype=torch.int32)
+    got = kernels.int4_repack(words.cuda()).cpu()
+    assert int(got[0, 0]) & 0xFFFFFFFF == 0x75316420
+    assert int(got[0, 1]) & 0xFFFFFFFF == 0xF0000000
+
+
 @pytest.mark.parametrize("fmt", ["g64", "g128z"])
 def test_int4_dequant_is_bit_exact(fmt: str) -> None:
     w = synthetic.normal(7, f"dq/{fmt}", (330, 512), 0.02)
     packed, _ = prod_int4.quantize_pack(w, fmt)
     dev = packed.to("cuda")
-    got = kernels.int4_dequant(dev.words, dev.scales, dev.zeros, packed.group)
+    got = kernels.int4_dequant(kernels.int4_repack(dev.words), dev.scales, dev.zeros, packed.group)
     zb = None if packed.zeros is None else bits(packed.zeros)
     want = int4_ref.dequantize_kernel_layout(packed.words.numpy(), bits(packed.scales), zb, packed.group)
     assert np.array_equal(bits(got), want)
@@ -139,6 +147,7 @@ def test_int4_lora_product_within_its_error_bound(fmt: str, m: int, k: int, outs
     adapters = torch.randint(0, pool_rows, (rows,), generator=g, dtype=torch.int32)
     x = torch.randn(m, k, generator=g).to(torch.bfloat16)
     dev = packed.to("cuda")
+    dev = prod_int4.PackedInt4(kernels.int4_repack(dev.words), dev.scales, dev.zeros, dev.group, dev.out)
     got = kernels.int4_product(x.cuda(), dev.words, dev.scales, dev.zeros, packed.group, sum(outs), a_pool.cuda(),
                                b_pool.cuda(), adapters.cuda(), row_len).cpu()
     row_of = adapters.long().repeat_interleave(row_len)
