@@ -220,7 +220,7 @@ def products_graph(path, b: int, n: int):
         for layer in f.layers:
             for key, x in (("proj", ws.h[:t]), ("out", ws.y[:t]), ("mlp_in", ws.h[:t]), ("mlp_down", ws.act[:t])):
                 lin = layer[key]
-                y = {"proj": ws.pr[:t * lin.out].view(t, lin.out), "out": ws.d[:t], "mlp_in": ws.gu[:t],
+                y = {"proj": ws.pr[:t * lin.out].view(t, lin.out), "out": ws.d[:t], "mlp_in": ws.act[:t],
                      "mlp_down": ws.d[:t]}[key]
                 lin(x, adapters, n, ws.mid, y)
                 flops += 2 * t * lin.k * lin.out + 2 * t * lin.rank * (lin.k + lin.out)

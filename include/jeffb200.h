@@ -25,8 +25,9 @@ extern "C" {
 #define JB_ECUDA (-2)    /* a CUDA runtime error */
 #define JB_ETIMEOUT (-3) /* a device-side bounded wait gave up (see jb_device_status) */
 #define JB_DEV_TIMEOUT 0x10000 /* device status word: a bounded wait gave up; low bits say where */
+#define JB_PRODUCT_SWIGLU 1    /* product flag: columns are gate|up blocks of 64; y = bf16(bf16(silu(g)) u) */
 
-/* ABI version of this header (bumped on any signature change). */
+/* ABI version of this header (bumped on any signature change): 2. */
 int jb_abi_version(void);
 /* The message of the last failure on the calling thread ("" if none). */
 const char* jb_last_error(void);
@@ -63,13 +64,17 @@ int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* lora_a, int 
  * (fast_path.py:347-349). */
 int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
                   const uint16_t* zeros, int group, int columns, int out, const uint16_t* mid, const uint16_t* lora_b,
-                  int rank, int pool_rows, const int32_t* adapters, int row_len, uint16_t* y, int ldy, void* stream);
+                  int rank, int pool_rows, const int32_t* adapters, int row_len, uint16_t* y, int ldy, int flags,
+                  void* stream);
 
-/* jb_lora_shrink then jb_w4a16_lora, with the caller's scratch `mid` (at least m * rank bf16). */
+/* jb_lora_shrink then jb_w4a16_lora, with the caller's scratch `mid` (at least m * rank bf16). flags: 0, or
+ * JB_PRODUCT_SWIGLU for a gate/up group whose columns are interleaved in blocks of 64 (gate 64, up 64, ...): then y
+ * (m, out / 2) = bf16(bf16(silu(g)) u) of the rounded products, the reference's silu_mul (fast_path.py:141-156)
+ * fused into the product's epilogue. */
 int jb_int4_lora_product(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
                          const uint16_t* zeros, int group, int columns, int out, const uint16_t* lora_a,
                          const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
-                         uint16_t* mid, uint16_t* y, int ldy, void* stream);
+                         uint16_t* mid, uint16_t* y, int ldy, int flags, void* stream);
 
 /* ---------------------------------------------------------------- fused norms and activations (S4) */
 
@@ -114,13 +119,20 @@ int jb_gdn_prep_rows(const uint16_t* pr, int ldpr, int t, int n, void* pool, int
                      void* stream);
 /* The gated delta rule over each row's n tokens from its state read in place from the pool (flat head
  * first_head + h at tables[r][(first_head + h) / heads_per_page], slot % heads_per_page); o (b, n, 16, 128) bf16.
- * last (nullable): stop after last[r] and write zeros past it. out_tables (nullable, the prefix pass): write each
- * row's final state into its own state pages. Replaces batched_kernels.gdn_recurrent_slots (:200-261) and fla's
- * chunk_gated_delta_rule at batched_path.py:282-288, :322-324. */
+ * Chunks of 64 tokens on tensor cores (bf16 operands, fp32 accumulation and state). last (nullable): outputs past
+ * last[r] are written as zeros. out_tables (nullable, the prefix pass): write each row's final state into its own
+ * state pages. Replaces fla's chunk_gated_delta_rule at batched_path.py:282-288, :322-324 (with the gathered initial
+ * states of batched_kernels.gather_gdn_states, :264-296, read in place instead). */
 int jb_gdn_scan(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g, const uint16_t* beta,
                 uint16_t* o, int b, int n, void* pool, int64_t page_bytes, const int32_t* tables, int table_stride,
                 int first_head, int heads_per_page, const int32_t* last, const int32_t* out_tables,
                 int out_table_stride, void* stream);
+/* The same rule token by token in fp32 (one value column per thread pair): the reference's
+ * batched_kernels.gdn_recurrent_slots (:200-261); last (nullable) stops after last[r], zeros past it. */
+int jb_gdn_scan_recurrent(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,
+                          const uint16_t* beta, uint16_t* o, int b, int n, void* pool, int64_t page_bytes,
+                          const int32_t* tables, int table_stride, int first_head, int heads_per_page,
+                          const int32_t* last, const int32_t* out_tables, int out_table_stride, void* stream);
 
 /* ---------------------------------------------------------------- attention (S3) */
 

@@ -72,7 +72,6 @@ class Workspace:
         self.ao = e(tokens, C.NQ, C.HD)
         self.kn = e(tokens, C.NKV, C.HD)
         self.vn = e(tokens, C.NKV, C.HD)
-        self.gu = e(tokens, 2 * C.INTER)
         self.act = e(tokens, C.INTER)
         self.mid = e(tokens * max(max_rank, 16))
         self.tables = torch.zeros(rows, width, dtype=torch.int32, device=device)
@@ -176,8 +175,7 @@ class BatchedPath:
                 ai += 1
             d = layer["out"](y, adapters, n, ws.mid, ws.d[:t])
             _, h = kernels.add_rms(x, d, layer["norm_post"], xo=x, h=ws.h[:t])
-            gu = layer["mlp_in"](h, adapters, n, ws.mid, ws.gu[:t])
-            act = kernels.silu_mul(gu, out=ws.act[:t])
+            act = layer["mlp_in"](h, adapters, n, ws.mid, ws.act[:t])     # SwiGLU in the product's epilogue
             d = layer["mlp_down"](act, adapters, n, ws.mid, ws.d[:t])
             if trace is not None:
                 trace.append((x.float() + d.float()).to(DT))
@@ -294,6 +292,28 @@ class BatchedPath:
         out = (x.float() + d.float()).to(DT)
         torch.cuda.synchronize(self.device)
         return out
+
+    def last_layer_readout(self, x_in: torch.Tensor, b: int, n: int, part: Sequence[tuple[int, int, Row]],
+                           lengths: Sequence[int]) -> torch.Tensor:
+        """The last decoder layer, the final norm and the readout, eagerly, on the residual stream x_in (B * N, 1024)
+        bf16 entering the last layer: probabilities (B, 255). For parity tests."""
+        size = self.fill(b, n, part, lengths)
+        self.inp[:size].copy_(self.inp_host[:size])
+        f, ws = self.fast, self.ws
+        v = self.views(b, n)
+        t = b * n
+        tables = ws.tables[:b]
+        torch.index_select(self.pool.tables, 0, v["slots"], out=tables)
+        x = ws.x[:t]
+        x.copy_(x_in)
+        li = len(f.layers) - 1
+        d = self._layers(x, v["adapters"], n, t, tables, tables, v["pos"], v["last"], first=li, stop=li + 1)
+        assert d is not None
+        hidden = kernels.rms_last(x, d, v["last"], n, f.final_w1, out=ws.hidden[:b])
+        probs = kernels.readout_rows(hidden, f.readout_pool, f.temp_pool, v["adapters"], v["counts"],
+                                     out=ws.probs[:b]).clone()
+        torch.cuda.synchronize(self.device)
+        return probs
 
     # ------------------------------------------------------------ requests
 

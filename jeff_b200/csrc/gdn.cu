@@ -198,16 +198,17 @@ extern "C" int jb_gdn_prep_rows(const uint16_t* pr, int ldpr, int t, int n, void
   return check_launch("gdn prep_kernel");
 }
 
-extern "C" int jb_gdn_scan(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,
+extern "C" int jb_gdn_scan_recurrent(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,
                            const uint16_t* beta, uint16_t* o, int b, int n, void* pool, int64_t page_bytes,
                            const int32_t* tables, int table_stride, int first_head, int heads_per_page,
                            const int32_t* last, const int32_t* out_tables, int out_table_stride, void* stream) {
-  JB_REQUIRE(q && k && v && g && beta && o && pool && tables, "jb_gdn_scan: null pointer");
-  JB_REQUIRE(b > 0 && n > 0, "jb_gdn_scan: b %d, n %d", b, n);
+  JB_REQUIRE(q && k && v && g && beta && o && pool && tables, "jb_gdn_scan_recurrent: null pointer");
+  JB_REQUIRE(b > 0 && n > 0, "jb_gdn_scan_recurrent: b %d, n %d", b, n);
   JB_REQUIRE(heads_per_page > 0 && (int64_t)heads_per_page * (int64_t)gdn::STATE_BYTES <= page_bytes,
-             "jb_gdn_scan: %d heads per page do not fit pages of %lld bytes", heads_per_page, (long long)page_bytes);
+             "jb_gdn_scan_recurrent: %d heads per page do not fit pages of %lld bytes", heads_per_page,
+             (long long)page_bytes);
   JB_REQUIRE(first_head >= 0 && (first_head + gdn::NH - 1) / heads_per_page < table_stride,
-             "jb_gdn_scan: heads %d.. reach past the block table (%d entries)", first_head, table_stride);
+             "jb_gdn_scan_recurrent: heads %d.. reach past the block table (%d entries)", first_head, table_stride);
   gdn::scan_kernel<<<b * gdn::NH, 256, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
       reinterpret_cast<const __nv_bfloat16*>(v), g, reinterpret_cast<const __nv_bfloat16*>(beta),

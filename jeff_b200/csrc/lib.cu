@@ -87,9 +87,10 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 #include "w4a16_gemm.cu"
 #include "elementwise.cu"
 #include "gdn.cu"
+#include "gdn_chunk.cu"
 #include "attention.cu"
 
-extern "C" int jb_abi_version(void) { return 1; }
+extern "C" int jb_abi_version(void) { return 2; }
 
 extern "C" const char* jb_last_error(void) { return jb::g_error; }
 

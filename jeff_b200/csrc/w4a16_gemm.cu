@@ -1,19 +1,24 @@
-// S1: the int4 W4A16 product fused with the per-row multi-LoRA update, tcgen05 + TMA (sm_100a).
+// S1: the int4 W4A16 product fused with the per-row multi-LoRA update, tcgen05 + TMA (sm_100a), persistent.
 //
 // y (M, out) = bf16( x (M, K) . W^T + mid . B[a]^T ), W = bf16(fp32(u - z) * fp32(s)) from int4 words in the kernel
 // layout (jb_int4_repack of the reference's layout: within each word the nibbles of inputs 0,2,4,6,1,3,5,7, so one
 // shift and one mask give two neighbouring inputs), scales/zeros (K/G, columns) bf16.
 //
-// One CTA computes a 256 x 128 tile (two 128-row halves sharing every dequantised weight tile) with 10 warps:
-//   warp 0      TMA producer: per 64-wide K block the x tile (256 x 64 bf16, 128B swizzle), the packed words
-//               (8 x 128 int32) and the group's scale (and zero) row, into a STAGES-deep ring (mbarrier full[s]);
-//   warp 1      allocates 256 TMEM columns; one thread issues tcgen05.mma (M=128, N=128, K=16) 4 x 2 per K block
-//               into the two fp32 accumulators and commits each stage back to the producer (empty[s]);
-//   warps 2-9   dequantise each stage's words (thread: one column, four words) into bf16 in the UMMA 128B-swizzled
-//               K-major layout (deq[s]); then the epilogue: the LoRA expand operands (each half's mid rows placed in
-//               their adapter's rank block, and the adapters' B rows) written over the idle rings, 1-12 more MMAs
-//               per half into the same accumulators, TMEM -> registers -> bf16 -> swizzled smem -> TMA store
-//               (clipped to M x out).
+// One CTA per SM loops over 256 x 128 output tiles (two 128-row halves sharing every dequantised weight tile), tile
+// index n-tile major so concurrent CTAs share weight tiles in L2. 14 warps:
+//   warp 0       TMA producer: per 64-wide K block the x tile (256 x 64 bf16, 128B swizzle), the packed words
+//                (8 x 128 int32) and the group's scale (and zero) row into a STAGES-deep ring (mbarrier full[s]);
+//   warp 1       allocates 512 TMEM columns (two 256-column accumulators, so a tile's epilogue overlaps the next
+//                tile's main loop); one thread issues tcgen05.mma (M=128, N=128, K=16) x 4 x 2 per K block;
+//   warps 2-9    two groups of four, each on alternate K blocks (two stages dequantised at once): each stage's
+//                words into bf16 in the UMMA 128B-swizzled K-major layout (deq[s]); for
+//                the LoRA expand they instead fill the x slot with each row's mid placed in its adapter's rank block
+//                and the weight slot with those adapters' B rows: the expand runs as extra K blocks of the same
+//                accumulator (columns [half 0 adapters | half 1 adapters], zeros elsewhere: exact);
+//   warps 10-13  epilogue: TMEM -> registers -> bf16 -> 16-byte stores of each row (clipped to M x out), then the
+//                accumulator is released (tmem_empty). With `swiglu` the 128 columns are 64 gate | 64 up columns of
+//                the interleaved gate/up group and the tile's 64 outputs are bf16(bf16(silu(g)) u) (the reference's
+//                silu_mul, fast_path.py:141-156, on the rounded products).
 // The base product is summed in fp32 in K order; the LoRA term joins the same fp32 accumulator; one rounding at the
 // end: the reference's cut-product rule (int4_kernels.py:1-30). No atomics: the result is deterministic.
 //
@@ -24,14 +29,16 @@
 namespace jb {
 namespace w4 {
 
-constexpr int BM = 256;             // rows per CTA (two UMMA halves of 128)
+constexpr int BM = 256;             // rows per tile (two UMMA halves of 128)
 constexpr int HM = 128;             // rows per half
 constexpr int BN = 128;
 constexpr int BK = 64;
 constexpr int STAGES = 4;
+constexpr int GROUPS = 2;          // dequantiser groups, each on alternate K blocks
 constexpr int DEQ_WARPS = 8;
-constexpr int THREADS = 64 + DEQ_WARPS * 32;
-constexpr int MAX_EXPAND = 192;     // adapters per half x rank: columns of the expand operand (<= 3 swizzle atoms)
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = 64 + (DEQ_WARPS + EPI_WARPS) * 32;
+constexpr int MAX_EXPAND = 192;     // adapters per half x rank (the expand uses twice that: both halves' adapters)
 
 struct Params {
   int M, K, columns, out, group;
@@ -39,6 +46,10 @@ struct Params {
   const __nv_bfloat16* lora_b;   // (pool_rows, columns, rank)
   const int* adapters;
   int rank, row_len, pool_rows;
+  int swiglu;                    // 1: columns are interleaved gate|up blocks of 64; y holds silu(g) u, out/2 wide
+  int m_tiles, n_tiles;
+  __nv_bfloat16* y;
+  int ldy;
   int* err;
 };
 
@@ -53,13 +64,10 @@ struct Layout {
   static constexpr int OFF_SC = OFF_RAW + STAGES * RAW_BYTES;
   static constexpr int OFF_ZR = OFF_SC + STAGES * SC_BYTES;
   static constexpr int OFF_BAR = OFF_ZR + STAGES * SC_BYTES;
-  static constexpr int NBAR = 3 * STAGES + 3;
+  static constexpr int NBAR = 3 * STAGES + 4;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int BYTES = OFF_MISC + 16;
   static constexpr int ALLOC = BYTES + 1024;       // room to align the base to 1024 B
-  static constexpr int SCRATCH = STAGES * (X_BYTES + W_BYTES);   // x and weight rings, contiguous, reused
-  static_assert(SCRATCH >= 4 * 3 * 16384, "rings too small for the LoRA expand operands");
-  static_assert(SCRATCH >= BM * BN * 2, "rings too small for the output staging");
   static_assert(ALLOC <= 227 * 1024, "shared memory");
 };
 
@@ -84,11 +92,13 @@ __device__ __forceinline__ __nv_bfloat162 zero_pair(const __nv_bfloat16* zr, int
   return __floats2bfloat162_rn(128.0f + z, 128.0f + z);
 }
 
+__device__ __forceinline__ float silu_rounded(float g) { return round_bf(g / (1.0f + expf(-g))); }
+
 template <bool ZERO>
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_lora_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                       const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
-                      const __grid_constant__ CUtensorMap tm_y, Params p) {
+                      Params p) {
   using L = Layout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -96,34 +106,33 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint64_t* full = bars;
   uint64_t* deq = bars + STAGES;
   uint64_t* empty = bars + 2 * STAGES;
-  uint64_t* main_done = bars + 3 * STAGES;
-  uint64_t* lora_ready = main_done + 1;
-  uint64_t* acc_full = main_done + 2;
+  uint64_t* tmem_full = bars + 3 * STAGES;       // [2]
+  uint64_t* tmem_empty = tmem_full + 2;          // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 4);
   volatile int* epi_ok = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 8);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BM;
-  const int n0 = blockIdx.y * BN;
   const int nkb = p.K / BK;
   const bool has_lora = p.mid != nullptr && p.rank > 0;
   const int n_adp = p.row_len >= HM ? 1 : HM / p.row_len;   // adapters per 128-row half
-  const int ke = has_lora ? n_adp * p.rank : 0;              // expand K (multiple of 16)
-  const int ke_pad = (ke + 63) & ~63;
-  const int atom_bytes_a = (ke_pad / 64) * HM * 128;         // one half's expand A operand
-  const int atom_bytes_b = (ke_pad / 64) * BN * 128;         // one half's expand B operand
+  const int ke_half = has_lora ? n_adp * p.rank : 0;         // expand columns per half
+  const int ke = 2 * ke_half;                                 // both halves' adapters
+  const int nlb = (ke + BK - 1) / BK;                         // LoRA K blocks
+  const int nkt = nkb + nlb;                                  // K blocks per tile
+  const int tiles = p.m_tiles * p.n_tiles;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&deq[s], DEQ_WARPS);
+      mbar_init(&deq[s], DEQ_WARPS / GROUPS);
       mbar_init(&empty[s], 1);
     }
-    mbar_init(main_done, 1);
-    mbar_init(lora_ready, 1);
-    mbar_init(acc_full, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], EPI_WARPS);
+    }
     *abort_flag = 0;
     *epi_ok = 0;
     fence_barrier_init();
@@ -133,10 +142,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tmap(&tm_w);
     prefetch_tmap(&tm_s);
     if (ZERO) prefetch_tmap(&tm_z);
-    prefetch_tmap(&tm_y);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 2 * BN);
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -145,158 +153,208 @@ __global__ void __launch_bounds__(THREADS, 1)
   const uint32_t tmem = *tmem_slot;
 
   if (warp == 0) {
+    // ---------------- producer
     if (lane == 0) {
       const uint32_t bytes = L::X_BYTES + L::RAW_BYTES + L::SC_BYTES * (ZERO ? 2 : 1);
-      for (int kb = 0; kb < nkb; ++kb) {
-        const int s = kb % STAGES;
-        if (kb >= STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort_flag, p.err, 1)) break;
-        mbar_arrive_expect_tx(&full[s], bytes);
-        tma_load_2d(smem + L::OFF_X + s * L::X_BYTES, &tm_x, &full[s], kb * BK, m0);
-        tma_load_2d(smem + L::OFF_RAW + s * L::RAW_BYTES, &tm_w, &full[s], n0, kb * (BK / 8));
-        tma_load_2d(smem + L::OFF_SC + s * L::SC_BYTES, &tm_s, &full[s], n0, (kb * BK) / p.group);
-        if (ZERO) tma_load_2d(smem + L::OFF_ZR + s * L::SC_BYTES, &tm_z, &full[s], n0, (kb * BK) / p.group);
+      uint32_t kg = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+        const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
+        for (int kb = 0; kb < nkt; ++kb, ++kg) {
+          const int s = kg % STAGES;
+          if (!mbar_wait(&empty[s], ((kg / STAGES) & 1) ^ 1, abort_flag, p.err, 1)) break;
+          if (kb < nkb) {
+            mbar_arrive_expect_tx(&full[s], bytes);
+            tma_load_2d(smem + L::OFF_X + s * L::X_BYTES, &tm_x, &full[s], kb * BK, m0);
+            tma_load_2d(smem + L::OFF_RAW + s * L::RAW_BYTES, &tm_w, &full[s], n0, kb * (BK / 8));
+            tma_load_2d(smem + L::OFF_SC + s * L::SC_BYTES, &tm_s, &full[s], n0, (kb * BK) / p.group);
+            if (ZERO) tma_load_2d(smem + L::OFF_ZR + s * L::SC_BYTES, &tm_z, &full[s], n0, (kb * BK) / p.group);
+          } else {
+            mbar_arrive(&full[s]);   // a LoRA block: the stage is free; the dequantisers fill it
+          }
+        }
       }
     }
   } else if (warp == 1) {
+    // ---------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_bf16(HM, BN);
+      uint32_t kg = 0;
+      int it = 0;
       bool ok = true;
-      for (int kb = 0; kb < nkb && ok; ++kb) {
-        const int s = kb % STAGES;
-        const uint32_t ph = (kb / STAGES) & 1;
-        ok = mbar_wait(&full[s], ph, abort_flag, p.err, 2) && mbar_wait(&deq[s], ph, abort_flag, p.err, 3);
+      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++it) {
+        const int b = it & 1;
+        ok = mbar_wait(&tmem_empty[b], ((it >> 1) & 1) ^ 1, abort_flag, p.err, 2);
         if (!ok) break;
         tc_fence_after();
-        const uint64_t a0 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES));
-        const uint64_t a1 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES + HM * 128));
-        const uint64_t bd = sw128_desc(smem_u32(smem + L::OFF_W + s * L::W_BYTES));
+        const uint32_t acc = tmem + b * 2 * BN;
+        for (int kb = 0; kb < nkt; ++kb, ++kg) {
+          const int s = kg % STAGES;
+          const uint32_t ph = (kg / STAGES) & 1;
+          ok = mbar_wait(&full[s], ph, abort_flag, p.err, 3) && mbar_wait(&deq[s], ph, abort_flag, p.err, 4);
+          if (!ok) break;
+          tc_fence_after();
+          const uint64_t a0 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES));
+          const uint64_t a1 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES + HM * 128));
+          const uint64_t bd = sw128_desc(smem_u32(smem + L::OFF_W + s * L::W_BYTES));
 #pragma unroll
-        for (int kk = 0; kk < BK / 16; ++kk) {
-          tc_mma_bf16(tmem, a0 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
-          tc_mma_bf16(tmem + BN, a1 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            tc_mma_bf16(acc, a0 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+            tc_mma_bf16(acc + BN, a1 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+          }
+          tc_commit(&empty[s]);
         }
-        tc_commit(&empty[s]);
+        if (!ok) break;
+        tc_commit(&tmem_full[b]);
       }
-      tc_commit(main_done);
-      if (ok && mbar_wait(lora_ready, 0, abort_flag, p.err, 4)) {
-        tc_fence_after();
-        for (int h = 0; h < 2; ++h) {
-          uint8_t* mid_t = smem + L::OFF_X + h * atom_bytes_a;
-          uint8_t* b_t = smem + L::OFF_X + 2 * atom_bytes_a + h * atom_bytes_b;
-          for (int j = 0; j < ke / 16; ++j) {
-            const int atom = j >> 2, w16 = j & 3;
-            const uint64_t ad = sw128_desc(smem_u32(mid_t + atom * HM * 128)) + 2 * w16;
-            const uint64_t bd = sw128_desc(smem_u32(b_t + atom * BN * 128)) + 2 * w16;
-            tc_mma_bf16(tmem + h * BN, ad, bd, idesc, 1);
+    }
+  } else if (warp < 2 + DEQ_WARPS) {
+    // ---------------- dequantisers: two groups of 128 threads, group g on the K blocks with kg % 2 == g
+    const int et = threadIdx.x - 64;
+    const int grp = et >> 7;
+    const int n = et & (BN - 1);            // this thread's weight column
+    uint32_t kg = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+      const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
+      for (int kb = 0; kb < nkt; ++kb, ++kg) {
+        if ((int)(kg % GROUPS) != grp) continue;
+        const int s = kg % STAGES;
+        ok = mbar_wait(&full[s], (kg / STAGES) & 1, abort_flag, p.err, 5);
+        if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+        uint8_t* wt = smem + L::OFF_W + s * L::W_BYTES;
+        if (kb < nkb) {
+          const int32_t* raw = reinterpret_cast<const int32_t*>(smem + L::OFF_RAW + s * L::RAW_BYTES);
+          const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(smem + L::OFF_SC + s * L::SC_BYTES);
+          const __nv_bfloat16* zr =
+              ZERO ? reinterpret_cast<const __nv_bfloat16*>(smem + L::OFF_ZR + s * L::SC_BYTES) : nullptr;
+          const __nv_bfloat162 s2 = __bfloat162bfloat162(sc[n]);
+          const __nv_bfloat162 zb2 = zero_pair(zr, n);
+          uint32_t w[8];
+#pragma unroll
+          for (int r = 0; r < 8; ++r) w[r] = static_cast<uint32_t>(raw[r * BN + n]);
+#pragma unroll
+          for (int r = 0; r < 8; ++r)
+            *reinterpret_cast<uint4*>(wt + sw128_offset(n, r)) = dequant8(w[r], s2, zb2);
+        } else {
+          // LoRA block: expand columns [col0, col0 + 64) of [half 0 adapters | half 1 adapters]
+          const int col0 = (kb - nkb) * BK;
+          // x slot: rows et & 127 of both halves get their mid in their adapter's block
+#pragma unroll 1
+          for (int h = 0; h < 2; ++h) {
+            const int lrow = n;
+            const int gm = m0 + h * HM + lrow;
+            const int block_of_row = h * n_adp + ((p.row_len >= HM) ? 0 : lrow / p.row_len);
+            uint8_t* xt = smem + L::OFF_X + s * L::X_BYTES + h * (HM * 128);
+#pragma unroll 1
+            for (int c8 = 0; c8 < 8; ++c8) {
+              const int col = col0 + 8 * c8;
+              uint4 v = make_uint4(0, 0, 0, 0);
+              if (col < ke && gm < p.M && col / p.rank == block_of_row)
+                v = *reinterpret_cast<const uint4*>(p.mid + (size_t)gm * p.rank + (col % p.rank));
+              *reinterpret_cast<uint4*>(xt + sw128_offset(lrow, c8)) = v;
+            }
+          }
+          // weight slot: column n holds the B rows of each block's adapter
+          const int gn = n0 + n;
+#pragma unroll 1
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const int col = col0 + 8 * c8;
+            uint4 v = make_uint4(0, 0, 0, 0);
+            if (col < ke && gn < p.columns) {
+              const int blk = col / p.rank;
+              const int hh = blk / n_adp, j = blk % n_adp;
+              const int first_row = m0 + hh * HM + j * (p.row_len >= HM ? 0 : p.row_len);
+              if (first_row < p.M) {
+                const int a = p.adapters[first_row / p.row_len];
+                if (a >= 0 && a < p.pool_rows)
+                  v = *reinterpret_cast<const uint4*>(p.lora_b + ((size_t)a * p.columns + gn) * p.rank +
+                                                      (col % p.rank));
+              }
+            }
+            *reinterpret_cast<uint4*>(wt + sw128_offset(n, c8)) = v;
           }
         }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&deq[s]);
       }
-      tc_commit(acc_full);
     }
   } else {
-    // ---------------- dequantisers (thread: column n, words 4 wh .. 4 wh + 3), then the epilogue: 256 threads
-    const int et = threadIdx.x - 64;
-    const int n = et & (BN - 1);
-    const int wh = et >> 7;
-    for (int kb = 0; kb < nkb; ++kb) {
-      const int s = kb % STAGES;
-      const bool ok = mbar_wait(&full[s], (kb / STAGES) & 1, abort_flag, p.err, 5);
-      if (!__all_sync(0xffffffffu, ok)) break;
-      const int32_t* raw = reinterpret_cast<const int32_t*>(smem + L::OFF_RAW + s * L::RAW_BYTES);
-      const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(smem + L::OFF_SC + s * L::SC_BYTES);
-      const __nv_bfloat16* zr = ZERO ? reinterpret_cast<const __nv_bfloat16*>(smem + L::OFF_ZR + s * L::SC_BYTES)
-                                     : nullptr;
-      uint8_t* wt = smem + L::OFF_W + s * L::W_BYTES;
-      const __nv_bfloat162 s2 = __bfloat162bfloat162(sc[n]);
-      const __nv_bfloat162 zb2 = zero_pair(zr, n);
-      uint32_t w[4];
-#pragma unroll
-      for (int r = 0; r < 4; ++r) w[r] = static_cast<uint32_t>(raw[(4 * wh + r) * BN + n]);
-#pragma unroll
-      for (int r = 0; r < 4; ++r)
-        *reinterpret_cast<uint4*>(wt + sw128_offset(n, 4 * wh + r)) = dequant8(w[r], s2, zb2);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&deq[s]);
-    }
-
-    // ---------------- epilogue: thread = row (half h, TMEM lane quadrant of its warp)
-    const int h = (warp - 2) >> 2;
-    const int lrow = 32 * (warp & 3) + lane;       // row within the half = its TMEM lane
-    const int row = h * HM + lrow;
-    if (et == 0) *epi_ok = mbar_wait(main_done, 0, abort_flag, p.err, 6) ? 1 : 0;
-    named_barrier(1, DEQ_WARPS * 32);
-    const bool go = *epi_ok != 0;
-    if (go && has_lora) {
-      // this half's mid rows into their adapter block of its expand A operand (over the consumed rings)
-      const int gm = m0 + row;
-      const int block_of_row = (p.row_len >= HM) ? 0 : (lrow / p.row_len);
-      uint8_t* mid_t = smem + L::OFF_X + h * atom_bytes_a;
-      for (int c8 = 0; c8 < ke_pad / 8; ++c8) {
-        const int col = c8 * 8;
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (col < ke && gm < p.M && col / p.rank == block_of_row)
-          v = *reinterpret_cast<const uint4*>(p.mid + (size_t)gm * p.rank + (col % p.rank));
-        *reinterpret_cast<uint4*>(mid_t + (col >> 6) * (HM * 128) + sw128_offset(lrow, (col & 63) >> 3)) = v;
-      }
-      // the B rows of the half's adapters: thread et builds column et & 127 of half et >> 7
-      {
-        const int bh = et >> 7;
-        const int bn = et & (BN - 1);
-        const int gn = n0 + bn;
-        uint8_t* b_t = smem + L::OFF_X + 2 * atom_bytes_a + bh * atom_bytes_b;
-        const int first_row_block = (m0 + bh * HM) / p.row_len;
-        for (int c8 = 0; c8 < ke_pad / 8; ++c8) {
-          const int col = c8 * 8;
-          uint4 v = make_uint4(0, 0, 0, 0);
-          const int blk = col / p.rank;
-          if (col < ke && gn < p.columns && (first_row_block + blk) * p.row_len < p.M &&
-              m0 + bh * HM < p.M) {
-            const int a = p.adapters[first_row_block + blk];
-            if (a >= 0 && a < p.pool_rows)
-              v = *reinterpret_cast<const uint4*>(p.lora_b + ((size_t)a * p.columns + gn) * p.rank + (col % p.rank));
-          }
-          *reinterpret_cast<uint4*>(b_t + (col >> 6) * (BN * 128) + sw128_offset(bn, (col & 63) >> 3)) = v;
-        }
-      }
-      fence_proxy_async_smem();
-    }
-    named_barrier(1, DEQ_WARPS * 32);
-    if (et == 0) mbar_arrive(lora_ready);
-    if (et == 0) *epi_ok = (go && mbar_wait(acc_full, 0, abort_flag, p.err, 7)) ? 1 : 0;
-    named_barrier(1, DEQ_WARPS * 32);
-    if (*epi_ok) {
+    // ---------------- epilogue: 128 threads; thread = row lrow of both halves (its TMEM lane); direct stores
+    const int et = threadIdx.x - 64 - DEQ_WARPS * 32;
+    const int lrow = 32 * (warp & 3) + lane;
+    const uint32_t lane_bits = (uint32_t)(32 * (warp & 3)) << 16;
+    __nv_bfloat16* y = p.y;
+    const int ow = p.swiglu ? p.out / 2 : p.out;      // output columns
+    int it = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+      const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
+      const int b = it & 1;
+      if (et == 0) *epi_ok = mbar_wait(&tmem_full[b], (it >> 1) & 1, abort_flag, p.err, 6) ? 1 : 0;
+      named_barrier(2, EPI_WARPS * 32);
+      if (!*epi_ok) break;
       tc_fence_after();
-      uint8_t* out_t = smem + L::OFF_X + h * (HM * BN * 2);   // per half: two 128 x 64 swizzled tiles
-      const uint32_t lane_addr = tmem + h * BN + ((uint32_t)(32 * (warp & 3)) << 16);
+      const uint32_t acc = tmem + b * 2 * BN + lane_bits;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(lane_addr + c * 32, r);
-        tc_wait_ld();
-        const int half64 = (c * 32) >> 6;
-        const int chunk0 = ((c * 32) & 63) >> 3;
+      for (int h = 0; h < 2; ++h) {
+        const int gm = m0 + h * HM + lrow;
+        __nv_bfloat16* yrow = y + (size_t)gm * p.ldy;
+        if (!p.swiglu) {
+#pragma unroll 1
+          for (int c = 0; c < BN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld32(acc + h * BN + c * 32, r);
+            tc_wait_ld();
+            if (gm < p.M) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          uint4 v;
-          v.x = pack_bf2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
-          v.y = pack_bf2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
-          v.z = pack_bf2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
-          v.w = pack_bf2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
-          *reinterpret_cast<uint4*>(out_t + half64 * 16384 + sw128_offset(lrow, chunk0 + q)) = v;
+              for (int q = 0; q < 4; ++q) {
+                const int col = n0 + c * 32 + q * 8;
+                if (col < ow) {
+                  uint4 v;
+                  v.x = pack_bf2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
+                  v.y = pack_bf2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
+                  v.z = pack_bf2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
+                  v.w = pack_bf2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
+                  *reinterpret_cast<uint4*>(yrow + col) = v;
+                }
+              }
+            }
+          }
+        } else {
+#pragma unroll 1
+          for (int c = 0; c < 2; ++c) {
+            uint32_t rg[32], ru[32];
+            tmem_ld32(acc + h * BN + c * 32, rg);
+            tmem_ld32(acc + h * BN + 64 + c * 32, ru);
+            tc_wait_ld();
+            if (gm < p.M) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const int col = n0 / 2 + c * 32 + q * 8;
+                float o[8];
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                  const float g = round_bf(__uint_as_float(rg[8 * q + e]));
+                  const float u = round_bf(__uint_as_float(ru[8 * q + e]));
+                  o[e] = silu_rounded(g) * u;
+                }
+                if (col < ow) {
+                  uint4 v;
+                  v.x = pack_bf2(o[0], o[1]);
+                  v.y = pack_bf2(o[2], o[3]);
+                  v.z = pack_bf2(o[4], o[5]);
+                  v.w = pack_bf2(o[6], o[7]);
+                  *reinterpret_cast<uint4*>(yrow + col) = v;
+                }
+              }
+            }
+          }
         }
       }
-      fence_proxy_async_smem();
-      named_barrier(1, DEQ_WARPS * 32);
-      if (et == 0) {
-        for (int hh = 0; hh < 2; ++hh) {
-          if (m0 + hh * HM >= p.M) continue;
-          for (int c = 0; c < BN / 64; ++c)
-            if (n0 + c * 64 < p.out)
-              tma_store_2d(&tm_y, smem + L::OFF_X + hh * (HM * BN * 2) + c * 16384, n0 + c * 64, m0 + hh * HM);
-        }
-        tma_store_commit_and_wait();
-      }
+      // the accumulator is read: release it to the MMA issuer for the tile after next
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tmem_empty[b]);
     }
   }
 
@@ -304,7 +362,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 2 * BN);
+    tmem_dealloc(tmem, 512);
   }
 }
 
@@ -386,18 +444,22 @@ __global__ void int4_dequant_kernel(const int32_t* __restrict__ words, const __n
 
 template <bool ZERO>
 int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz,
-           const CUtensorMap& ty, const Params& p, cudaStream_t stream) {
+           const Params& p, cudaStream_t stream) {
   auto kernel = w4a16_lora_kernel<ZERO>;
   static bool configured[64] = {};
+  static int sms[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !configured[dev]) {
     cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout::ALLOC);
     if (e != cudaSuccess) return status_of(e, "w4a16: cudaFuncSetAttribute");
+    e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return status_of(e, "w4a16: SM count");
     configured[dev] = true;
   }
-  dim3 grid((p.M + BM - 1) / BM, (p.columns + BN - 1) / BN);
-  kernel<<<grid, THREADS, Layout::ALLOC, stream>>>(tx, tw, ts, tz, ty, p);
+  const int tiles = p.m_tiles * p.n_tiles;
+  const int grid = tiles < sms[dev] ? tiles : sms[dev];
+  kernel<<<grid, THREADS, Layout::ALLOC, stream>>>(tx, tw, ts, tz, p);
   return check_launch("w4a16_lora_kernel");
 }
 
@@ -456,13 +518,19 @@ extern "C" int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* l
 extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
                              const uint16_t* zeros, int group, int columns, int out, const uint16_t* mid,
                              const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
-                             uint16_t* y, int ldy, void* stream) {
+                             uint16_t* y, int ldy, int flags, void* stream) {
+  const bool swiglu = (flags & JB_PRODUCT_SWIGLU) != 0;
+  const int yw = swiglu ? out / 2 : out;   // output columns
   JB_REQUIRE(x && words && scales && y, "jb_w4a16_lora: null pointer");
   JB_REQUIRE(m > 0 && k > 0 && k % 64 == 0, "jb_w4a16_lora: m %d, k %d (k a multiple of 64)", m, k);
   JB_REQUIRE(columns > 0 && columns % 64 == 0 && out > 0 && out <= columns,
              "jb_w4a16_lora: columns %d (multiple of 64), out %d <= columns", columns, out);
+  JB_REQUIRE(!swiglu || (columns % w4::BN == 0 && out == columns),
+             "jb_w4a16_lora: the SwiGLU epilogue needs interleaved gate|up blocks filling whole 128-column tiles "
+             "(columns %d, out %d)", columns, out);
   JB_REQUIRE(group == 64 || group == 128, "jb_w4a16_lora: group %d (64 or 128)", group);
-  JB_REQUIRE(ldy >= out && ldy % 8 == 0, "jb_w4a16_lora: ldy %d must be >= out and a multiple of 8", ldy);
+  JB_REQUIRE(out % 8 == 0, "jb_w4a16_lora: out %d must be a multiple of 8", out);
+  JB_REQUIRE(ldy >= yw && ldy % 8 == 0, "jb_w4a16_lora: ldy %d must be >= %d and a multiple of 8", ldy, yw);
   JB_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0 &&
                  (reinterpret_cast<uintptr_t>(words) & 15) == 0 && (reinterpret_cast<uintptr_t>(scales) & 15) == 0,
              "jb_w4a16_lora: x, y, words and scales must be 16-byte aligned");
@@ -477,7 +545,7 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
                rank, w4::MAX_EXPAND);
     JB_REQUIRE(pool_rows > 0, "jb_w4a16_lora: pool_rows %d", pool_rows);
   }
-  CUtensorMap tx, tw, ts, tz, ty;
+  CUtensorMap tx, tw, ts, tz;
   int st;
   constexpr int BN = w4::BN;
   if ((st = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, m, (uint64_t)k * 2, 64, w4::BM,
@@ -497,15 +565,13 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
   } else {
     tz = ts;
   }
-  if ((st = make_tmap_2d(&ty, y, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, out, m, (uint64_t)ldy * 2, 64, w4::HM,
-                         CU_TENSOR_MAP_SWIZZLE_128B)))
-    return st;
   w4::Params p{m, k, columns, out, group,
                lora ? reinterpret_cast<const __nv_bfloat16*>(mid) : nullptr,
                reinterpret_cast<const __nv_bfloat16*>(lora_b), adapters, lora ? rank : 0, row_len > 0 ? row_len : 128,
-               pool_rows, device_status_word()};
-  if (zeros) return w4::launch<true>(tx, tw, ts, tz, ty, p, (cudaStream_t)stream);
-  return w4::launch<false>(tx, tw, ts, tz, ty, p, (cudaStream_t)stream);
+               pool_rows, swiglu ? 1 : 0, (m + w4::BM - 1) / w4::BM, (columns + BN - 1) / BN,
+               reinterpret_cast<__nv_bfloat16*>(y), ldy, device_status_word()};
+  if (zeros) return w4::launch<true>(tx, tw, ts, tz, p, (cudaStream_t)stream);
+  return w4::launch<false>(tx, tw, ts, tz, p, (cudaStream_t)stream);
 }
 
 extern "C" int jb_int4_repack(const int32_t* words, int32_t* out, int k, int columns, void* stream) {
@@ -519,12 +585,12 @@ extern "C" int jb_int4_repack(const int32_t* words, int32_t* out, int k, int col
 extern "C" int jb_int4_lora_product(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
                                     const uint16_t* zeros, int group, int columns, int out, const uint16_t* lora_a,
                                     const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters,
-                                    int row_len, uint16_t* mid, uint16_t* y, int ldy, void* stream) {
+                                    int row_len, uint16_t* mid, uint16_t* y, int ldy, int flags, void* stream) {
   if (rank > 0) {
     JB_REQUIRE(mid && lora_a, "jb_int4_lora_product: LoRA needs lora_a and the mid scratch");
     int st = jb_lora_shrink(x, m, k, lora_a, rank, pool_rows, adapters, row_len, mid, stream);
     if (st) return st;
   }
   return jb_w4a16_lora(x, m, k, words, scales, zeros, group, columns, out, rank > 0 ? mid : nullptr, lora_b, rank,
-                       pool_rows, adapters, row_len, y, ldy, stream);
+                       pool_rows, adapters, row_len, y, ldy, flags, stream);
 }

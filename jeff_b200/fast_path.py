@@ -24,17 +24,36 @@ from jeff_b200.synthetic import AdapterWeights, FusedGroup, ModelWeights
 DT = torch.bfloat16
 
 
+def swiglu_order(inter: int, block: int = 64) -> torch.Tensor:
+    """Column order of a [gate | up] group for the fused SwiGLU epilogue: gate block j (64 columns), then up block
+    j, for j = 0 .. inter / 64 - 1, so every 128-column tile of the product holds matching gate and up columns."""
+    idx = []
+    for j in range(inter // block):
+        idx += list(range(j * block, (j + 1) * block)) + list(range(inter + j * block, inter + (j + 1) * block))
+    return torch.tensor(idx, dtype=torch.long)
+
+
 class DeviceLin:
-    def __init__(self, grp: FusedGroup, pool_rows: int, device: torch.device) -> None:
+    def __init__(self, grp: FusedGroup, pool_rows: int, device: torch.device, swiglu: bool = False) -> None:
         p = grp.packed
         self.names = grp.names
         self.k = grp.k
         self.out = grp.out
         self.group = p.group
         self.columns = p.columns
-        self.words = kernels.int4_repack(p.words.to(device))     # the kernels' word layout
-        self.scales = p.scales.to(device)
-        self.zeros = p.zeros.to(device) if p.zeros is not None else None
+        self.swiglu = swiglu
+        words, scales, zeros = p.words, p.scales, p.zeros
+        self.order: torch.Tensor | None = None
+        if swiglu:
+            if len(grp.sizes) != 2 or grp.sizes[0] != grp.sizes[1] or grp.sizes[0] % 64 or p.columns != grp.out:
+                raise ValueError(f"{', '.join(grp.names)}: the SwiGLU epilogue needs a [gate | up] group of equal "
+                                 "halves, a multiple of 64 wide")
+            self.order = swiglu_order(grp.sizes[0])
+            words, scales = words[:, self.order], scales[:, self.order]
+            zeros = zeros[:, self.order] if zeros is not None else None
+        self.words = kernels.int4_repack(words.contiguous().to(device))     # the kernels' word layout
+        self.scales = scales.contiguous().to(device)
+        self.zeros = zeros.contiguous().to(device) if zeros is not None else None
         self.rank = grp.rank
         self.lora_a = torch.zeros(pool_rows, self.rank, self.k, dtype=DT, device=device) if self.rank else None
         self.lora_b = torch.zeros(pool_rows, self.columns, self.rank, dtype=DT, device=device) if self.rank else None
@@ -49,6 +68,8 @@ class DeviceLin:
                              f"rank {self.rank}, {self.k} inputs, {self.out} outputs")
         self.lora_a[row].copy_(a)
         self.lora_b[row].zero_()
+        if self.order is not None:
+            b = b[self.order.to(b.device)]
         self.lora_b[row, :self.out].copy_(b)
 
     def clear(self, row: int) -> None:
@@ -62,7 +83,7 @@ class DeviceLin:
         m = x.shape[0]
         mid_v = mid[:m * self.rank].view(m, self.rank) if (mid is not None and self.rank) else None
         return kernels.int4_product(x, self.words, self.scales, self.zeros, self.group, self.out, self.lora_a,
-                                    self.lora_b, adapters, row_len, mid_v, y)
+                                    self.lora_b, adapters, row_len, mid_v, y, swiglu=self.swiglu)
 
     def nbytes(self) -> int:
         n = self.words.numel() * 4 + self.scales.numel() * 2 + (self.zeros.numel() * 2 if self.zeros is not None else 0)
@@ -89,7 +110,7 @@ class FastPath:
             layer: dict = {"kind": lw.kind, "norm_in": (1.0 + lw.norm_in.float()).to(dev),
                            "norm_post": (1.0 + lw.norm_post.float()).to(dev)}
             for key, grp in lw.groups.items():
-                lin = DeviceLin(grp, rows, dev)
+                lin = DeviceLin(grp, rows, dev, swiglu=(key == "mlp_in"))
                 layer[key] = lin
                 self.lins.append(lin)
             if lw.kind == "linear_attention":

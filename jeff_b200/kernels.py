@@ -69,22 +69,23 @@ def lora_shrink(x: torch.Tensor, lora_a: torch.Tensor, adapters: torch.Tensor, r
 def int4_product(x: torch.Tensor, words: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor | None, group: int,
                  out_features: int, lora_a: torch.Tensor | None, lora_b: torch.Tensor | None,
                  adapters: torch.Tensor | None, row_len: int, mid: torch.Tensor | None = None,
-                 y: torch.Tensor | None = None) -> torch.Tensor:
+                 y: torch.Tensor | None = None, swiglu: bool = False) -> torch.Tensor:
     """y (m, out) = bf16(x W^T + bf16(x A[a]^T) B[a]^T) for row a = adapters[t // row_len] of token t: the fused
     product of one group (module docstring); `words` in the kernel layout (int4_repack). lora_a (rows, R, k),
-    lora_b (rows, columns, R) bf16, or None."""
+    lora_b (rows, columns, R) bf16, or None. swiglu: the group's columns are gate|up blocks of 64 and y (m, out / 2)
+    receives bf16(bf16(silu(g)) u) (fast_path.silu_mul fused into the epilogue)."""
     m, k = x.shape
     columns = words.shape[1]
     if words.shape[0] * 8 != k:
         raise ValueError(f"int4_product: x has {k} inputs, the weights {words.shape[0] * 8}")
     rank = 0 if lora_a is None else lora_a.shape[1]
     if y is None:
-        y = torch.empty(m, out_features, dtype=DT, device=x.device)
+        y = torch.empty(m, out_features // 2 if swiglu else out_features, dtype=DT, device=x.device)
     if rank and mid is None:
         mid = torch.empty(m, rank, dtype=DT, device=x.device)
     _lib.call("jb_int4_lora_product", ptr(x), m, k, ptr(words), ptr(scales), ptr(zeros), group, columns, out_features,
               ptr(lora_a), ptr(lora_b), rank, 0 if lora_a is None else lora_a.shape[0], ptr(adapters), row_len,
-              ptr(mid) if rank else None, ptr(y), y.stride(0), stream_ptr())
+              ptr(mid) if rank else None, ptr(y), y.stride(0), 1 if swiglu else 0, stream_ptr())
     return y
 
 
@@ -194,8 +195,10 @@ def gdn_prep_rows(pr: torch.Tensor, pool, tables: torch.Tensor, gdn_layer: int, 
 
 def gdn_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor, pool,
              tables: torch.Tensor, gdn_layer: int, last: torch.Tensor | None = None,
-             out_tables: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
-    """The gated delta rule from each row's pooled state (batched_kernels.gdn_recurrent_slots); o (B, n, 16, 128)."""
+             out_tables: torch.Tensor | None = None, out: torch.Tensor | None = None,
+             kernel: str = "chunk") -> torch.Tensor:
+    """The gated delta rule from each row's pooled state; o (B, n, 16, 128). kernel "chunk" (64-token chunks on
+    tensor cores, fla's chunk_gated_delta_rule) or "recurrent" (token by token, batched_kernels.gdn_recurrent_slots)."""
     b, n = q.shape[:2]
     shapes = pool.shapes
     if tables.dim() != 2 or tables.shape[0] < b or tables.shape[1] < shapes.fixed_pages or tables.dtype != torch.int32:
@@ -205,7 +208,8 @@ def gdn_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
         if not x.is_contiguous():
             raise ValueError(f"gdn_scan: {name} must be contiguous")
     o = out if out is not None else torch.empty_like(v)
-    _lib.call("jb_gdn_scan", ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), ptr(o), b, n, ptr(pool.data),
+    name = {"chunk": "jb_gdn_scan", "recurrent": "jb_gdn_scan_recurrent"}[kernel]
+    _lib.call(name, ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), ptr(o), b, n, ptr(pool.data),
               shapes.page_bytes, ptr(tables), tables.stride(0), shapes.state[0] * gdn_layer, shapes.heads_per_page,
               ptr(last), ptr(out_tables), 0 if out_tables is None else out_tables.stride(0), stream_ptr())
     return o

@@ -23,13 +23,13 @@ def test_every_declared_entry_point_is_exported(lib: ctypes.CDLL) -> None:
     assert len(names) >= 19
     for name in names:
         assert hasattr(lib, name), name
-    assert lib.jb_abi_version() == 1
+    assert lib.jb_abi_version() == 2
 
 
 def test_bad_arguments_are_refused_before_any_launch(lib: ctypes.CDLL) -> None:
     p = ctypes.c_void_p(16)
     # k not a multiple of 64
-    assert lib.jb_w4a16_lora(p, 64, 100, p, p, None, 64, 128, 128, None, None, 0, 0, None, 64, p, 128, None) == -1
+    assert lib.jb_w4a16_lora(p, 64, 100, p, p, None, 64, 128, 128, None, None, 0, 0, None, 64, p, 128, 0, None) == -1
     assert b"multiple of 64" in lib.jb_last_error()
     # group must be 64 or 128
     assert lib.jb_int4_dequant(p, p, None, 128, 128, 32, p, None) == -1
@@ -39,7 +39,7 @@ def test_bad_arguments_are_refused_before_any_launch(lib: ctypes.CDLL) -> None:
                                 None) == -1
     assert b"rows of 32" in lib.jb_last_error()
     # the LoRA tile constraint: rows per tile x rank <= 192
-    assert lib.jb_w4a16_lora(p, 128, 1024, p, p, None, 64, 128, 128, p, p, 64, 3, p, 32, p, 128, None) == -1
+    assert lib.jb_w4a16_lora(p, 128, 1024, p, p, None, 64, 128, 128, p, p, 64, 3, p, 32, p, 128, 0, None) == -1
     assert b"exceeds" in lib.jb_last_error()
     with pytest.raises(_lib.ArgumentError, match="rank 20"):
         _lib.call("jb_lora_shrink", p, 32, 64, p, 20, 1, p, 32, p, None)

@@ -131,6 +131,7 @@ def exact_product(x: torch.Tensor, W: torch.Tensor, a_rows, b_rows, row_of: torc
     (256, 1024, [4096, 512, 512], 128),           # the attention projection (q+gate, k, v)
     (192, 2048, [1024], 64),                      # out_proj, ragged M (not a multiple of 128)
     (96, 3584, [1024], 32),                       # down_proj, k = 3584
+    (2048, 1024, [3584], 128),                    # many tiles per persistent CTA
 ])
 def test_int4_lora_product_within_its_error_bound(fmt: str, m: int, k: int, outs: list[int], row_len: int) -> None:
     g = torch.Generator().manual_seed(m + k + len(outs))
@@ -158,6 +159,35 @@ def test_int4_lora_product_within_its_error_bound(fmt: str, m: int, k: int, outs
     again = kernels.int4_product(x.cuda(), dev.words, dev.scales, dev.zeros, packed.group, sum(outs), a_pool.cuda(),
                                  b_pool.cuda(), adapters.cuda(), row_len).cpu()
     assert torch.equal(got, again)
+
+
+@pytest.mark.parametrize("fmt", ["g128z", "g64"])
+def test_int4_lora_product_swiglu_epilogue(fmt: str) -> None:
+    """The gate/up group with the SwiGLU epilogue (columns interleaved in blocks of 64): y = bf16(bf16(silu(g)) u)
+    of the rounded products. Against silu_mul of the exact products rounded to bf16: within four bf16 steps (a
+    product within its error bound can round to the neighbouring bf16 value, moving g or u by one step), and 5e-4
+    absolute where g or u is near zero (the products' float32 summation slack, about 1e-4 here, dominates there)."""
+    from jeff_b200.fast_path import swiglu_order
+
+    g = torch.Generator().manual_seed(77)
+    m, k, inter, row_len, rank, pool_rows = 512, 1024, 3584, 128, 32, 3
+    w = torch.randn(2 * inter, k, generator=g) * 0.02
+    packed, W = prod_int4.quantize_pack(w, fmt)
+    order = swiglu_order(inter)
+    a_pool = (torch.randn(pool_rows, rank, k, generator=g) * 0.02).to(torch.bfloat16)
+    b_pool = (torch.randn(pool_rows, 2 * inter, rank, generator=g) * 0.02).to(torch.bfloat16)
+    adapters = torch.randint(0, pool_rows, (m // row_len,), generator=g, dtype=torch.int32)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    zeros = None if packed.zeros is None else packed.zeros[:, order].contiguous().cuda()
+    words = kernels.int4_repack(packed.words[:, order].contiguous().cuda())
+    got = kernels.int4_product(x.cuda(), words, packed.scales[:, order].contiguous().cuda(), zeros, packed.group,
+                               2 * inter, a_pool.cuda(), b_pool[:, order].contiguous().cuda(), adapters.cuda(),
+                               row_len, swiglu=True).cpu().float()
+    row_of = adapters.long().repeat_interleave(row_len)
+    exact, _ = exact_product(x.float(), W.float(), a_pool.float(), b_pool.float(), row_of)
+    gu = bf(exact.float())
+    want = model_ref.silu_mul(gu)
+    torch.testing.assert_close(got, want, rtol=4 * BF16_STEP, atol=5e-4)
 
 
 def test_lora_shrink_matches_the_oracle() -> None:
@@ -275,46 +305,59 @@ def gdn_inputs(b: int, n: int, seed: int):
     return q, k, v, gg, beta
 
 
+@pytest.mark.parametrize("kernel", ["chunk", "recurrent"])
 @pytest.mark.parametrize("b", BATCHES)
-@pytest.mark.parametrize("n", [32, 64])
+@pytest.mark.parametrize("n", [32, 64, 160])
 @pytest.mark.parametrize("gdn_layer", [0, 5, 17])
-def test_gdn_scan_matches_the_oracle(pool_fixture, b: int, n: int, gdn_layer: int) -> None:
-    """Each row from its own prefix state read in place (layer 5's heads straddle pages). GDN_RTOL, GDN_ATOL (the
-    reference's: two bf16 steps at the largest outputs); with a stop at the last real token, the real positions are
-    bit for bit those without it and the padding positions zero."""
+def test_gdn_scan_matches_the_oracle(pool_fixture, kernel: str, b: int, n: int, gdn_layer: int) -> None:
+    """Each row from its own prefix state read in place (layer 5's heads straddle pages); n = 160 runs two whole
+    64-token chunks and a partial one. GDN_RTOL, GDN_ATOL (the reference's: two bf16 steps at the largest outputs,
+    set for fla's chunk kernel, whose bf16 operand roundings the chunk kernel shares); with a stop at the last real
+    token, the real positions are bit for bit those without it and the padding positions zero."""
     pool, slots, states = pool_fixture
     ss = pass_slots(slots, b, seed=b * 7 + n + gdn_layer)
     tables, _ = tables_for(pool, ss)
     q, k, v, g, beta = gdn_inputs(b, n, seed=b + n + gdn_layer)
-    got = kernels.gdn_scan(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), pool, tables, gdn_layer)
+    got = kernels.gdn_scan(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), pool, tables, gdn_layer,
+                           kernel=kernel)
     s0 = torch.stack([states[s][1][gdn_layer] for s in ss])
     want, _ = model_ref.gdn_scan(q.float(), k.float(), v.float(), g, beta.float(), s0)
     torch.testing.assert_close(got.cpu().float(), want, rtol=GDN_RTOL, atol=GDN_ATOL)
     rng = random.Random(b * n)
     last = torch.tensor([n - 1 if r == 0 else rng.randrange(n) for r in range(b)], dtype=torch.int32)
     stopped = kernels.gdn_scan(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), pool, tables, gdn_layer,
-                               last=last.cuda()).cpu()
+                               last=last.cuda(), kernel=kernel).cpu()
     for r in range(b):
         end = int(last[r]) + 1
         assert torch.equal(stopped[r, :end], got[r, :end].cpu())
         assert not stopped[r, end:].any()
 
 
-def test_gdn_scan_writes_the_final_state_into_the_output_pages(pool_fixture) -> None:
+@pytest.mark.parametrize("kernel", ["chunk", "recurrent"])
+def test_gdn_scan_writes_the_final_state_into_the_output_pages(pool_fixture, kernel: str) -> None:
+    """The prefix pass's final states: the recurrent kernel within float32 noise (rtol 1e-4); the chunk kernel,
+    whose state products take bf16 operands, within 1e-2 norm-wise per head."""
     pool, slots, states = pool_fixture
-    b, n = 3, 64
+    b, n = 3, 160
     ss = [slots[33], 0, slots[100]]
     tables, _ = tables_for(pool, ss)
     q, k, v, g, beta = gdn_inputs(b, n, seed=42)
-    fresh = [pool.reserve(2, f"out {i}", 40) for i in range(b)]
+    fresh = [pool.reserve(2, f"out {kernel} {i}", 40) for i in range(b)]
+    pool.pin(fresh)
     out_tables = pool.tables.index_select(0, torch.tensor(fresh, device="cuda")).contiguous()
-    kernels.gdn_scan(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), pool, tables, 7, out_tables=out_tables)
+    kernels.gdn_scan(q.cuda(), k.cuda(), v.cuda(), g.cuda(), beta.cuda(), pool, tables, 7, out_tables=out_tables,
+                     kernel=kernel)
     torch.cuda.synchronize()
     s0 = torch.stack([states[s][1][7] for s in ss])
     _, s_fin = model_ref.gdn_scan(q.float(), k.float(), v.float(), g, beta.float(), s0)
+    pool.unpin(fresh)
     for i, slot in enumerate(fresh):
         got = pool.gather(slot)[1][7].cpu()
-        torch.testing.assert_close(got, s_fin[i], rtol=1e-4, atol=1e-5)
+        if kernel == "recurrent":
+            torch.testing.assert_close(got, s_fin[i], rtol=1e-4, atol=1e-5)
+        else:
+            for hh in range(16):
+                assert model_ref.rel_error(got[hh], s_fin[i][hh]) < 1e-2
         pool.release(slot)
 
 
