@@ -236,43 +236,48 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int r = 0; r < 8; ++r)
             *reinterpret_cast<uint4*>(wt + sw128_offset(n, r)) = dequant8(w[r], s2, zb2);
         } else {
-          // LoRA block: expand columns [col0, col0 + 64) of [half 0 adapters | half 1 adapters]
+          // LoRA block: expand columns [col0, col0 + 64) of [half 0 adapters | half 1 adapters]. Every global load
+          // of the block is issued before any store, so their latencies overlap.
           const int col0 = (kb - nkb) * BK;
-          // x slot: rows et & 127 of both halves get their mid in their adapter's block
-#pragma unroll 1
+          const int lrow = n;
+          const int gn = n0 + n;
+          uint4 xv[2][8], wv[8];
+#pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int lrow = n;
             const int gm = m0 + h * HM + lrow;
             const int block_of_row = h * n_adp + ((p.row_len >= HM) ? 0 : lrow / p.row_len);
-            uint8_t* xt = smem + L::OFF_X + s * L::X_BYTES + h * (HM * 128);
-#pragma unroll 1
+#pragma unroll
             for (int c8 = 0; c8 < 8; ++c8) {
               const int col = col0 + 8 * c8;
-              uint4 v = make_uint4(0, 0, 0, 0);
+              xv[h][c8] = make_uint4(0, 0, 0, 0);
               if (col < ke && gm < p.M && col / p.rank == block_of_row)
-                v = *reinterpret_cast<const uint4*>(p.mid + (size_t)gm * p.rank + (col % p.rank));
-              *reinterpret_cast<uint4*>(xt + sw128_offset(lrow, c8)) = v;
+                xv[h][c8] = *reinterpret_cast<const uint4*>(p.mid + (size_t)gm * p.rank + (col % p.rank));
             }
           }
-          // weight slot: column n holds the B rows of each block's adapter
-          const int gn = n0 + n;
-#pragma unroll 1
+#pragma unroll
           for (int c8 = 0; c8 < 8; ++c8) {
             const int col = col0 + 8 * c8;
-            uint4 v = make_uint4(0, 0, 0, 0);
+            wv[c8] = make_uint4(0, 0, 0, 0);
             if (col < ke && gn < p.columns) {
               const int blk = col / p.rank;
               const int hh = blk / n_adp, j = blk % n_adp;
               const int first_row = m0 + hh * HM + j * (p.row_len >= HM ? 0 : p.row_len);
               if (first_row < p.M) {
-                const int a = p.adapters[first_row / p.row_len];
+                const int a = __ldg(p.adapters + first_row / p.row_len);
                 if (a >= 0 && a < p.pool_rows)
-                  v = *reinterpret_cast<const uint4*>(p.lora_b + ((size_t)a * p.columns + gn) * p.rank +
-                                                      (col % p.rank));
+                  wv[c8] = *reinterpret_cast<const uint4*>(p.lora_b + ((size_t)a * p.columns + gn) * p.rank +
+                                                           (col % p.rank));
               }
             }
-            *reinterpret_cast<uint4*>(wt + sw128_offset(n, c8)) = v;
           }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint8_t* xt = smem + L::OFF_X + s * L::X_BYTES + h * (HM * 128);
+#pragma unroll
+            for (int c8 = 0; c8 < 8; ++c8) *reinterpret_cast<uint4*>(xt + sw128_offset(lrow, c8)) = xv[h][c8];
+          }
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) *reinterpret_cast<uint4*>(wt + sw128_offset(n, c8)) = wv[c8];
         }
         fence_proxy_async_smem();
         __syncwarp();
