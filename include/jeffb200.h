@@ -26,6 +26,7 @@ extern "C" {
 #define JB_ETIMEOUT (-3) /* a device-side bounded wait gave up (see jb_device_status) */
 #define JB_DEV_TIMEOUT 0x10000 /* device status word: a bounded wait gave up; low bits say where */
 #define JB_PRODUCT_SWIGLU 1    /* product flag: columns are gate|up blocks of 64; y = bf16(bf16(silu(g)) u) */
+#define JB_PRODUCT_STATIC_MID_MAX 1048576 /* m * rank limit of jb_int4_lora_product_static (2 MiB of bf16) */
 
 /* ABI version of this header (bumped on any signature change): 2. */
 int jb_abi_version(void);
@@ -75,6 +76,20 @@ int jb_int4_lora_product(const uint16_t* x, int m, int k, const int32_t* words, 
                          const uint16_t* zeros, int group, int columns, int out, const uint16_t* lora_a,
                          const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
                          uint16_t* mid, uint16_t* y, int ldy, int flags, void* stream);
+
+/* jb_int4_lora_product without the `mid` argument, allocating nothing: the shrink's output goes to a scratch array
+ * fixed in the library's device memory (one per device, m * rank <= JB_PRODUCT_STATIC_MID_MAX; larger calls get
+ * JB_EINVAL). For callers that must not allocate device memory: a host binding the C ABI directly with no device
+ * allocator of its own, or one whose device memory its own pool reserves up front. The first call on a device
+ * looks up the array's address there (make it before any stream capture). Calls on one device must not overlap
+ * (two streams or two host threads at once): they share the scratch and race. The scratch needs no zeroing: the
+ * shrink writes all of it that the expand reads. This entry point has no counterpart in the reference, whose
+ * int4_product (int4_kernels.py:132-177) keeps the LoRA intermediate in a torch-allocated Workspace buffer (ws.QP)
+ * and allocates its output through torch on every call. */
+int jb_int4_lora_product_static(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
+                                const uint16_t* zeros, int group, int columns, int out, const uint16_t* lora_a,
+                                const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters,
+                                int row_len, uint16_t* y, int ldy, int flags, void* stream);
 
 /* ---------------------------------------------------------------- fused norms and activations (S4) */
 

@@ -599,3 +599,61 @@ extern "C" int jb_int4_lora_product(const uint16_t* x, int m, int k, const int32
   return jb_w4a16_lora(x, m, k, words, scales, zeros, group, columns, out, rank > 0 ? mid : nullptr, lora_b, rank,
                        pool_rows, adapters, row_len, y, ldy, flags, stream);
 }
+
+// ------------------------------------------------------------------ the product without caller scratch
+//
+// jb_int4_lora_product needs an (m, rank) bf16 scratch for the LoRA shrink's output. This variant takes none and
+// allocates nothing: the scratch is a fixed array in the library's own device memory, sized for the largest pass
+// the hot path runs (16384 tokens at rank 64). It serves callers that must not allocate device memory themselves:
+// a host that binds the C ABI directly and owns no device allocator, or one whose device memory is reserved up
+// front by its own pool. The array's address on each device is looked up once, by the first call made with that
+// device current; make that first call before any stream capture. There is one array per device, so calls on one
+// device must not overlap (two streams, or two host threads, at once): they would share the scratch and race.
+// Nothing in the array has to start at zero: the shrink writes every element the expand then reads, on the same
+// stream, before the expand launches.
+
+static __device__ __align__(256) uint16_t g_product_mid[JB_PRODUCT_STATIC_MID_MAX];
+
+static uint16_t* product_mid_scratch() {
+  static std::mutex mu;
+  static uint16_t* addr[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    status_of(e, "jb_int4_lora_product_static: cudaGetDevice");
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    set_error("jb_int4_lora_product_static: device %d out of range", dev);
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_product_mid);
+    if (e != cudaSuccess) {
+      status_of(e, "jb_int4_lora_product_static: scratch address");
+      return nullptr;
+    }
+    addr[dev] = static_cast<uint16_t*>(p);
+  }
+  return addr[dev];
+}
+
+extern "C" int jb_int4_lora_product_static(const uint16_t* x, int m, int k, const int32_t* words,
+                                           const uint16_t* scales, const uint16_t* zeros, int group, int columns,
+                                           int out, const uint16_t* lora_a, const uint16_t* lora_b, int rank,
+                                           int pool_rows, const int32_t* adapters, int row_len, uint16_t* y, int ldy,
+                                           int flags, void* stream) {
+  uint16_t* mid = nullptr;
+  if (rank > 0) {
+    JB_REQUIRE(m > 0 && (long long)m * rank <= JB_PRODUCT_STATIC_MID_MAX,
+               "jb_int4_lora_product_static: m %d x rank %d exceeds the static scratch of %d elements", m, rank,
+               JB_PRODUCT_STATIC_MID_MAX);
+    JB_REQUIRE(lora_a, "jb_int4_lora_product_static: LoRA needs lora_a");
+    mid = product_mid_scratch();
+    if (!mid) return JB_ECUDA;
+  }
+  return jb_int4_lora_product(x, m, k, words, scales, zeros, group, columns, out, lora_a, lora_b, rank, pool_rows,
+                              adapters, row_len, mid, y, ldy, flags, stream);
+}
