@@ -32,6 +32,12 @@ int* device_status_word();   // this device's status word (static device memory)
 // Encodes a 2-D tiled tensor map (driver entry point fetched through the runtime; no libcuda link needed).
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner, uint64_t outer,
                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+// A bf16 matrix (rows, cols) with 16-byte rows pieces, viewed as planes of 8 columns: dims {8, rows, cols / 8},
+// strides {row_bytes, 16}, box {8, box_rows, cols / 8}. One load lands as cols / 8 planes of box_rows x 16 B each
+// (the planes layout of planes_desc). Returns JB_OK, or an error status (with jb_last_error set) when the driver
+// does not take the map.
+int make_tmap_planes(CUtensorMap* map, const void* base, uint64_t rows, uint32_t cols, uint64_t row_bytes,
+                     uint32_t box_rows);
 
 // ------------------------------------------------------------------ device: bf16 helpers
 
@@ -118,6 +124,14 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(smem_u32(bar))
       : "memory");
 }
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::
+          "r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
@@ -191,6 +205,13 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
          ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Shared-memory matrix descriptor: K-major operand without swizzle, laid out as planes of 8 K-values: plane c holds
+// every row's inputs 8c .. 8c + 7 (16 B per row, rows contiguous), planes `plane_bytes` apart. Core matrices (8 rows
+// x 16 B) are then 128 B apart along M/N (SBO) and `plane_bytes` apart along K (LBO); layout SWIZZLE_NONE = 0.
+__device__ __forceinline__ uint64_t planes_desc(uint32_t saddr, uint32_t plane_bytes) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)((plane_bytes >> 4) & 0x3FFFu) << 16) |
+         ((uint64_t)(128 >> 4) << 32) | ((uint64_t)1 << 46);
 }
 // Instruction descriptor, kind::f16: f32 accumulator, bf16 A and B, both K-major, M and N.
 __host__ __device__ constexpr uint32_t idesc_bf16(int m, int n) {

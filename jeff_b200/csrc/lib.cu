@@ -82,6 +82,33 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   return JB_OK;
 }
 
+int make_tmap_planes(CUtensorMap* map, const void* base, uint64_t rows, uint32_t cols, uint64_t row_bytes,
+                     uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return JB_ECUDA;
+  }
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (row_bytes & 15) || cols % 8 || cols == 0 || cols > 64) {
+    set_error("planes map: base %p, row pitch %llu, %u columns (16-byte aligned, columns a multiple of 8 up to 64)",
+              base, (unsigned long long)row_bytes, cols);
+    return JB_EINVAL;
+  }
+  cuuint64_t dims[3] = {8, rows, cols / 8};
+  cuuint64_t strides[2] = {row_bytes, 16};
+  cuuint32_t box[3] = {8, box_rows, cols / 8};
+  cuuint32_t elem[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, elem,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled (planes) failed (%d): %llu rows x %u columns, pitch %llu", (int)r,
+              (unsigned long long)rows, cols, (unsigned long long)row_bytes);
+    return JB_ECUDA;
+  }
+  return JB_OK;
+}
+
 }  // namespace jb
 
 #include "w4a16_gemm.cu"

@@ -11,10 +11,12 @@
 //   warp 1       allocates 512 TMEM columns (two 256-column accumulators, so a tile's epilogue overlaps the next
 //                tile's main loop); one thread issues tcgen05.mma (M=128, N=128, K=16) x 4 x 2 per K block;
 //   warps 2-9    two groups of four, each on alternate K blocks (two stages dequantised at once): each stage's
-//                words into bf16 in the UMMA 128B-swizzled K-major layout (deq[s]); for
-//                the LoRA expand they instead fill the x slot with each row's mid placed in its adapter's rank block
-//                and the weight slot with those adapters' B rows: the expand runs as extra K blocks of the same
-//                accumulator (columns [half 0 adapters | half 1 adapters], zeros elsewhere: exact);
+//                words into bf16 in the UMMA 128B-swizzled K-major layout (deq[s]).
+// The LoRA expand runs as extra K blocks of the same accumulator: the x slot holds each row's mid in its
+// adapter's rank block and the weight slot those adapters' B rows (columns [half 0 adapters | half 1 adapters],
+// zeros elsewhere: exact). With one adapter per 128-row half (rows of >= 128 tokens) the producer instead loads each
+// half's mid rows and its adapter's B rows by TMA as planes of 8 columns, and each half's expand is an MMA of its own
+// (no zero blocks); otherwise the dequantisers gather the block-diagonal operands.
 //   warps 10-13  epilogue: TMEM -> registers -> bf16 -> 16-byte stores of each row (clipped to M x out), then the
 //                accumulator is released (tmem_empty). With `swiglu` the 128 columns are 64 gate | 64 up columns of
 //                the interleaved gate/up group and the tile's 64 outputs are bf16(bf16(silu(g)) u) (the reference's
@@ -51,6 +53,7 @@ struct Params {
   __nv_bfloat16* y;
   int ldy;
   int* err;
+  int planes3d;                  // 1: tm_mid / tm_lb load every plane of a half at once; 0: one plane per load
 };
 
 struct Layout {
@@ -66,7 +69,9 @@ struct Layout {
   static constexpr int OFF_BAR = OFF_ZR + STAGES * SC_BYTES;
   static constexpr int NBAR = 3 * STAGES + 4;
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-  static constexpr int BYTES = OFF_MISC + 16;
+  static constexpr int OFF_ADP = OFF_MISC + 16;
+  static constexpr int MAX_ROWS = 512;            // adapter indices staged in shared memory (M / row_len rows)
+  static constexpr int BYTES = OFF_ADP + MAX_ROWS * 4;
   static constexpr int ALLOC = BYTES + 1024;       // room to align the base to 1024 B
   static_assert(ALLOC <= 227 * 1024, "shared memory");
 };
@@ -98,6 +103,7 @@ template <bool ZERO>
 __global__ void __launch_bounds__(THREADS, 1)
     w4a16_lora_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                       const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
+                      const __grid_constant__ CUtensorMap tm_mid, const __grid_constant__ CUtensorMap tm_lb,
                       Params p) {
   using L = Layout;
   extern __shared__ uint8_t smem_raw[];
@@ -119,9 +125,22 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int n_adp = p.row_len >= HM ? 1 : HM / p.row_len;   // adapters per 128-row half
   const int ke_half = has_lora ? n_adp * p.rank : 0;         // expand columns per half
   const int ke = 2 * ke_half;                                 // both halves' adapters
-  const int nlb = (ke + BK - 1) / BK;                         // LoRA K blocks
+  // one adapter per 128-row half (row_len >= 128): the producer loads each half's mid rows and its adapter's B
+  // rows by TMA, and each half's expand is its own MMA of depth rank (both halves in one K block when 2 rank <= 64,
+  // else one block each); otherwise the dequantisers gather block-diagonal operands (see below)
+  const bool lora_tma = has_lora && p.row_len >= HM;
+  const bool halves_together = 2 * p.rank <= BK;
+  const int nlb = lora_tma ? (halves_together ? 1 : 2) : (ke + BK - 1) / BK;   // LoRA K blocks
   const int nkt = nkb + nlb;                                  // K blocks per tile
   const int tiles = p.m_tiles * p.n_tiles;
+  int* s_adp = reinterpret_cast<int*>(smem + L::OFF_ADP);
+  if (has_lora) {
+    const int rows = (p.M + p.row_len - 1) / p.row_len;
+    for (int i = threadIdx.x; i < rows && i < L::MAX_ROWS; i += blockDim.x) {
+      const int a = p.adapters[i];
+      s_adp[i] = (a >= 0 && a < p.pool_rows) ? a : -1;
+    }
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -142,6 +161,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tmap(&tm_w);
     prefetch_tmap(&tm_s);
     if (ZERO) prefetch_tmap(&tm_z);
+    if (has_lora && p.row_len >= HM) {
+      prefetch_tmap(&tm_mid);
+      prefetch_tmap(&tm_lb);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, 512);
@@ -168,6 +191,29 @@ __global__ void __launch_bounds__(THREADS, 1)
             tma_load_2d(smem + L::OFF_RAW + s * L::RAW_BYTES, &tm_w, &full[s], n0, kb * (BK / 8));
             tma_load_2d(smem + L::OFF_SC + s * L::SC_BYTES, &tm_s, &full[s], n0, (kb * BK) / p.group);
             if (ZERO) tma_load_2d(smem + L::OFF_ZR + s * L::SC_BYTES, &tm_z, &full[s], n0, (kb * BK) / p.group);
+          } else if (lora_tma) {
+            // a LoRA block by TMA: for each of its halves, the half's mid rows (rank / 8 planes of 128 rows x 16 B)
+            // into the x slot and its adapter's B rows for this column tile into the weight slot. Rows past m and
+            // an invalid adapter read outside the tensors: zeros.
+            const int h_lo = halves_together ? 0 : kb - nkb, h_hi = halves_together ? 2 : h_lo + 1;
+            const int planes = p.rank / 8;
+            mbar_arrive_expect_tx(&full[s], 2 * (h_hi - h_lo) * planes * 2048);
+            for (int h = h_lo; h < h_hi; ++h) {
+              uint8_t* xd = smem + L::OFF_X + s * L::X_BYTES + (h - h_lo) * (HM * 128);
+              uint8_t* wd = smem + L::OFF_W + s * L::W_BYTES + (h - h_lo) * planes * 2048;
+              const int row0 = m0 + h * HM;
+              const int a = row0 < p.M ? s_adp[row0 / p.row_len] : -1;
+              const int brow0 = a >= 0 ? a * p.columns + n0 : p.pool_rows * p.columns;
+              if (p.planes3d) {
+                tma_load_3d(xd, &tm_mid, &full[s], 0, row0, 0);
+                tma_load_3d(wd, &tm_lb, &full[s], 0, brow0, 0);
+              } else {
+                for (int c = 0; c < planes; ++c) {
+                  tma_load_2d(xd + c * 2048, &tm_mid, &full[s], 8 * c, row0);
+                  tma_load_2d(wd + c * 2048, &tm_lb, &full[s], 8 * c, brow0);
+                }
+              }
+            }
           } else {
             mbar_arrive(&full[s]);   // a LoRA block: the stage is free; the dequantisers fill it
           }
@@ -193,13 +239,25 @@ __global__ void __launch_bounds__(THREADS, 1)
           ok = mbar_wait(&full[s], ph, abort_flag, p.err, 3) && mbar_wait(&deq[s], ph, abort_flag, p.err, 4);
           if (!ok) break;
           tc_fence_after();
-          const uint64_t a0 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES));
-          const uint64_t a1 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES + HM * 128));
-          const uint64_t bd = sw128_desc(smem_u32(smem + L::OFF_W + s * L::W_BYTES));
+          if (kb >= nkb && lora_tma) {
+            // each half against its own adapter, planes layout: K16 step j reads planes 2j, 2j + 1
+            const int h_lo = halves_together ? 0 : kb - nkb, h_hi = halves_together ? 2 : h_lo + 1;
+            for (int h = h_lo; h < h_hi; ++h) {
+              const uint32_t xa = smem_u32(smem + L::OFF_X + s * L::X_BYTES + (h - h_lo) * (HM * 128));
+              const uint32_t wa = smem_u32(smem + L::OFF_W + s * L::W_BYTES + (h - h_lo) * (p.rank / 8) * 2048);
+              for (int j = 0; j < p.rank / 16; ++j)
+                tc_mma_bf16(acc + h * BN, planes_desc(xa + 2 * j * 2048, 2048), planes_desc(wa + 2 * j * 2048, 2048),
+                            idesc, 1);
+            }
+          } else {
+            const uint64_t a0 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES));
+            const uint64_t a1 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES + HM * 128));
+            const uint64_t bd = sw128_desc(smem_u32(smem + L::OFF_W + s * L::W_BYTES));
 #pragma unroll
-          for (int kk = 0; kk < BK / 16; ++kk) {
-            tc_mma_bf16(acc, a0 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
-            tc_mma_bf16(acc + BN, a1 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+            for (int kk = 0; kk < BK / 16; ++kk) {
+              tc_mma_bf16(acc, a0 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+              tc_mma_bf16(acc + BN, a1 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+            }
           }
           tc_commit(&empty[s]);
         }
@@ -235,7 +293,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int r = 0; r < 8; ++r)
             *reinterpret_cast<uint4*>(wt + sw128_offset(n, r)) = dequant8(w[r], s2, zb2);
-        } else {
+        } else if (!lora_tma) {
           // LoRA block: expand columns [col0, col0 + 64) of [half 0 adapters | half 1 adapters]. Every global load
           // of the block is issued before any store, so their latencies overlap.
           const int col0 = (kb - nkb) * BK;
@@ -263,8 +321,8 @@ __global__ void __launch_bounds__(THREADS, 1)
               const int hh = blk / n_adp, j = blk % n_adp;
               const int first_row = m0 + hh * HM + j * (p.row_len >= HM ? 0 : p.row_len);
               if (first_row < p.M) {
-                const int a = __ldg(p.adapters + first_row / p.row_len);
-                if (a >= 0 && a < p.pool_rows)
+                const int a = s_adp[first_row / p.row_len];
+                if (a >= 0)
                   wv[c8] = *reinterpret_cast<const uint4*>(p.lora_b + ((size_t)a * p.columns + gn) * p.rank +
                                                            (col % p.rank));
               }
@@ -449,7 +507,7 @@ __global__ void int4_dequant_kernel(const int32_t* __restrict__ words, const __n
 
 template <bool ZERO>
 int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz,
-           const Params& p, cudaStream_t stream) {
+           const CUtensorMap& tm, const CUtensorMap& tl, const Params& p, cudaStream_t stream) {
   auto kernel = w4a16_lora_kernel<ZERO>;
   static bool configured[64] = {};
   static int sms[64] = {};
@@ -464,7 +522,7 @@ int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ts, 
   }
   const int tiles = p.m_tiles * p.n_tiles;
   const int grid = tiles < sms[dev] ? tiles : sms[dev];
-  kernel<<<grid, THREADS, Layout::ALLOC, stream>>>(tx, tw, ts, tz, p);
+  kernel<<<grid, THREADS, Layout::ALLOC, stream>>>(tx, tw, ts, tz, tm, tl, p);
   return check_launch("w4a16_lora_kernel");
 }
 
@@ -550,7 +608,7 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
                rank, w4::MAX_EXPAND);
     JB_REQUIRE(pool_rows > 0, "jb_w4a16_lora: pool_rows %d", pool_rows);
   }
-  CUtensorMap tx, tw, ts, tz;
+  CUtensorMap tx, tw, ts, tz, tm, tl;
   int st;
   constexpr int BN = w4::BN;
   if ((st = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, m, (uint64_t)k * 2, 64, w4::BM,
@@ -570,13 +628,36 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
   } else {
     tz = ts;
   }
+  if (lora) {
+    JB_REQUIRE((m + row_len - 1) / row_len <= w4::Layout::MAX_ROWS, "jb_w4a16_lora: more than %d rows",
+               w4::Layout::MAX_ROWS);
+    JB_REQUIRE((reinterpret_cast<uintptr_t>(mid) & 15) == 0 && (reinterpret_cast<uintptr_t>(lora_b) & 15) == 0,
+               "jb_w4a16_lora: mid and lora_b must be 16-byte aligned");
+  }
+  int planes3d = 0;
+  if (lora && row_len >= w4::HM) {
+    // the planes maps; where the driver refuses them, 2D maps of one plane per load
+    planes3d = make_tmap_planes(&tm, mid, m, rank, (uint64_t)rank * 2, w4::HM) == JB_OK &&
+               make_tmap_planes(&tl, lora_b, (uint64_t)pool_rows * columns, rank, (uint64_t)rank * 2, w4::BN) == JB_OK;
+    if (!planes3d) {
+      if ((st = make_tmap_2d(&tm, mid, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, m, (uint64_t)rank * 2, 8, w4::HM,
+                             CU_TENSOR_MAP_SWIZZLE_NONE)))
+        return st;
+      if ((st = make_tmap_2d(&tl, lora_b, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, (uint64_t)pool_rows * columns,
+                             (uint64_t)rank * 2, 8, w4::BN, CU_TENSOR_MAP_SWIZZLE_NONE)))
+        return st;
+    }
+  } else {
+    tm = tx;
+    tl = tx;
+  }
   w4::Params p{m, k, columns, out, group,
                lora ? reinterpret_cast<const __nv_bfloat16*>(mid) : nullptr,
                reinterpret_cast<const __nv_bfloat16*>(lora_b), adapters, lora ? rank : 0, row_len > 0 ? row_len : 128,
                pool_rows, swiglu ? 1 : 0, (m + w4::BM - 1) / w4::BM, (columns + BN - 1) / BN,
-               reinterpret_cast<__nv_bfloat16*>(y), ldy, device_status_word()};
-  if (zeros) return w4::launch<true>(tx, tw, ts, tz, p, (cudaStream_t)stream);
-  return w4::launch<false>(tx, tw, ts, tz, p, (cudaStream_t)stream);
+               reinterpret_cast<__nv_bfloat16*>(y), ldy, device_status_word(), planes3d};
+  if (zeros) return w4::launch<true>(tx, tw, ts, tz, tm, tl, p, (cudaStream_t)stream);
+  return w4::launch<false>(tx, tw, ts, tz, tm, tl, p, (cudaStream_t)stream);
 }
 
 extern "C" int jb_int4_repack(const int32_t* words, int32_t* out, int k, int columns, void* stream) {

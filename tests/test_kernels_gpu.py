@@ -132,6 +132,7 @@ def exact_product(x: torch.Tensor, W: torch.Tensor, a_rows, b_rows, row_of: torc
     (192, 2048, [1024], 64),                      # out_proj, ragged M (not a multiple of 128)
     (96, 3584, [1024], 32),                       # down_proj, k = 3584
     (2048, 1024, [3584], 128),                    # many tiles per persistent CTA
+    (384, 1024, [1024], 128),                     # a tile whose second 128-row half lies past m
 ])
 def test_int4_lora_product_within_its_error_bound(fmt: str, m: int, k: int, outs: list[int], row_len: int) -> None:
     g = torch.Generator().manual_seed(m + k + len(outs))
