@@ -18,8 +18,21 @@ __device__ __forceinline__ float warp_sum(float v) {
   return v;
 }
 
-// grid (t, 3): part 0 q heads, 1 k heads, 2 v heads; 16 warps, warp = head, lane = 4 channels
-__global__ void __launch_bounds__(512) prep_kernel(const __nv_bfloat16* __restrict__ pr, int ldpr, int n,
+// Sliding window over tokens: grid (ceil(chunks / 4), 49, rows), 4 warps per block, warp = a chunk of PT tokens of
+// one row. Slices 0-47: the 128 channels of one q, k or v head (slice / 16 = part, slice % 16 = head), lane = 4
+// channels; the lane keeps its 4 x 4 conv taps and its last three inputs in registers, so every input is read once.
+// Slice 48: the gates g and beta of the chunk's tokens (lanes = 2 tokens x 16 heads).
+constexpr int PT = 32;
+
+__device__ __forceinline__ void load4(const __nv_bfloat16* src, float (&x)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(src);
+  x[0] = bf_lo(u.x);
+  x[1] = bf_hi(u.x);
+  x[2] = bf_lo(u.y);
+  x[3] = bf_hi(u.y);
+}
+
+__global__ void __launch_bounds__(128) prep_kernel(const __nv_bfloat16* __restrict__ pr, int ldpr, int n,
                                                    uint8_t* __restrict__ pool, int64_t page_bytes,
                                                    const int* __restrict__ tables, int table_stride, int conv_entry,
                                                    int conv_slot, const float* __restrict__ conv_w,
@@ -28,63 +41,92 @@ __global__ void __launch_bounds__(512) prep_kernel(const __nv_bfloat16* __restri
                                                    __nv_bfloat16* __restrict__ v, float* __restrict__ g,
                                                    __nv_bfloat16* __restrict__ beta, const int* __restrict__ real,
                                                    const int* __restrict__ out_tables, int out_table_stride) {
-  const int t = blockIdx.x;
-  const int part = blockIdx.y;
-  const int head = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int row = t / n, tt = t - row * n;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = blockIdx.z, slice = blockIdx.y;
+  const int t0 = (blockIdx.x * 4 + warp) * PT;
+  if (t0 >= n) return;
+  const int t1 = min(t0 + PT, n);
+  const size_t rbase = (size_t)row * n;
+  if (slice == 3 * NH) {
+    const int h = lane & 15;
+    const float an = a_neg[h], db = dt_bias[h];
+    const int rl = real ? real[row] : n;
+    for (int tt = t0 + (lane >> 4); tt < t1; tt += 2) {
+      const size_t t = rbase + tt;
+      const float bv = __bfloat162float(pr[t * ldpr + OFF_B + h]);
+      const float av = __bfloat162float(pr[t * ldpr + OFF_A + h]) + db;
+      const float sp = av > 20.0f ? av : logf(1.0f + expf(av));
+      float gv = an * sp;
+      float bt = 1.0f / (1.0f + expf(-bv));
+      if (tt >= rl) {
+        gv = 0.f;
+        bt = 0.f;
+      }
+      g[t * NH + h] = gv;
+      beta[t * NH + h] = __float2bfloat16_rn(bt);
+    }
+    return;
+  }
+  const int part = slice / NH, head = slice % NH;
   const int ch = part * 2048 + head * HDIM + lane * 4;
   const int page = tables[(size_t)row * table_stride + conv_entry];
   const __nv_bfloat16* tail = reinterpret_cast<const __nv_bfloat16*>(pool + (int64_t)page * page_bytes +
                                                                       conv_slot * CONV_BYTES);
-  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float w[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const int s = tt + i;   // index in [3 cached inputs; new inputs]
-    const __nv_bfloat16* src = s < 3 ? tail + (size_t)s * QKV + ch : pr + (size_t)(t + i - 3) * ldpr + ch;
-    const uint2 xu = *reinterpret_cast<const uint2*>(src);
-    const float xv[4] = {bf_lo(xu.x), bf_hi(xu.x), bf_lo(xu.y), bf_hi(xu.y)};
-    const float4 w = *reinterpret_cast<const float4*>(conv_w + (size_t)i * QKV + ch);
-    acc[0] += w.x * xv[0];
-    acc[1] += w.y * xv[1];
-    acc[2] += w.z * xv[2];
-    acc[3] += w.w * xv[3];
+    const float4 wv = *reinterpret_cast<const float4*>(conv_w + (size_t)i * QKV + ch);
+    w[i][0] = wv.x;
+    w[i][1] = wv.y;
+    w[i][2] = wv.z;
+    w[i][3] = wv.w;
   }
-  float c[4];
+  // inputs at positions t0 - 3 .. t0 - 1 of [3 cached; new]
+  float x0[4], x1[4], x2[4];
+  {
+    const int p0 = t0 - 3, p1 = t0 - 2, p2 = t0 - 1;
+    load4(p0 < 0 ? tail + (size_t)(p0 + 3) * QKV + ch : pr + (rbase + p0) * ldpr + ch, x0);
+    load4(p1 < 0 ? tail + (size_t)(p1 + 3) * QKV + ch : pr + (rbase + p1) * ldpr + ch, x1);
+    load4(p2 < 0 ? tail + (size_t)(p2 + 3) * QKV + ch : pr + (rbase + p2) * ldpr + ch, x2);
+  }
+  __nv_bfloat16* dst = part == 0 ? q : (part == 1 ? k : v);
+#pragma unroll 4
+  for (int tt = t0; tt < t1; ++tt) {
+    float x3[4];
+    load4(pr + (rbase + tt) * ldpr + ch, x3);
+    float c[4];
 #pragma unroll
-  for (int e = 0; e < 4; ++e) c[e] = round_bf(acc[e] / (1.0f + expf(-acc[e])));
-  const size_t o = ((size_t)t * NH + head) * HDIM + lane * 4;
-  if (part < 2) {
-    const float ss = warp_sum(c[0] * c[0] + c[1] * c[1] + c[2] * c[2] + c[3] * c[3]);
-    const float rs = rsqrtf(ss + 1e-6f);
-    const uint2 outv = make_uint2(pack_bf2(c[0] * rs, c[1] * rs), pack_bf2(c[2] * rs, c[3] * rs));
-    *reinterpret_cast<uint2*>((part == 0 ? q : k) + o) = outv;
-  } else {
-    *reinterpret_cast<uint2*>(v + o) = make_uint2(pack_bf2(c[0], c[1]), pack_bf2(c[2], c[3]));
-  }
-  if (part == 0 && head == 0 && lane < NH) {
-    const float bv = __bfloat162float(pr[(size_t)t * ldpr + OFF_B + lane]);
-    const float av = __bfloat162float(pr[(size_t)t * ldpr + OFF_A + lane]) + dt_bias[lane];
-    const float sp = av > 20.0f ? av : logf(1.0f + expf(av));
-    float gv = a_neg[lane] * sp;
-    float bt = 1.0f / (1.0f + expf(-bv));
-    if (real && tt >= real[row]) {
-      gv = 0.f;
-      bt = 0.f;
+    for (int e = 0; e < 4; ++e) {
+      float acc = 0.f;
+      acc += w[0][e] * x0[e];
+      acc += w[1][e] * x1[e];
+      acc += w[2][e] * x2[e];
+      acc += w[3][e] * x3[e];
+      c[e] = round_bf(acc / (1.0f + expf(-acc)));
+      x0[e] = x1[e];
+      x1[e] = x2[e];
+      x2[e] = x3[e];
     }
-    g[(size_t)t * NH + lane] = gv;
-    beta[(size_t)t * NH + lane] = __float2bfloat16_rn(bt);
+    const size_t o = ((rbase + tt) * NH + head) * HDIM + lane * 4;
+    if (part < 2) {
+      const float ss = warp_sum(c[0] * c[0] + c[1] * c[1] + c[2] * c[2] + c[3] * c[3]);
+      const float rs = rsqrtf(ss + 1e-6f);
+      *reinterpret_cast<uint2*>(dst + o) = make_uint2(pack_bf2(c[0] * rs, c[1] * rs), pack_bf2(c[2] * rs, c[3] * rs));
+    } else {
+      *reinterpret_cast<uint2*>(dst + o) = make_uint2(pack_bf2(c[0], c[1]), pack_bf2(c[2], c[3]));
+    }
   }
-  if (real && out_tables && tt == 0) {
+  if (real && out_tables && t0 == 0) {
     // the prefix pass: this row's last three real convolution inputs become its cached tail
     const int r = real[row];
     const int opage = out_tables[(size_t)row * out_table_stride + conv_entry];
     __nv_bfloat16* otail = reinterpret_cast<__nv_bfloat16*>(pool + (int64_t)opage * page_bytes + conv_slot * CONV_BYTES);
 #pragma unroll
     for (int i = 0; i < 3; ++i) {
-      const int s = r + i;
+      const int pos = r - 3 + i;
       uint2 val;
-      if (s < 3) val = *reinterpret_cast<const uint2*>(tail + (size_t)s * QKV + ch);
-      else val = *reinterpret_cast<const uint2*>(pr + (size_t)(row * n + s - 3) * ldpr + ch);
+      if (pos < 0) val = *reinterpret_cast<const uint2*>(tail + (size_t)(pos + 3) * QKV + ch);
+      else val = *reinterpret_cast<const uint2*>(pr + (rbase + pos) * ldpr + ch);
       *reinterpret_cast<uint2*>(otail + (size_t)i * QKV + ch) = val;
     }
   }
@@ -189,8 +231,9 @@ extern "C" int jb_gdn_prep_rows(const uint16_t* pr, int ldpr, int t, int n, void
                  (int64_t)(conv_slot + 1) * (int64_t)gdn::CONV_BYTES <= page_bytes,
              "jb_gdn_prep_rows: conv entry %d / slot %d do not fit the page geometry", conv_entry, conv_slot);
   JB_REQUIRE(!out_tables || real, "jb_gdn_prep_rows: out_tables needs real");
-  dim3 grid(t, 3);
-  gdn::prep_kernel<<<grid, 512, 0, (cudaStream_t)stream>>>(
+  const int chunks = (n + gdn::PT - 1) / gdn::PT;
+  dim3 grid((chunks + 3) / 4, 3 * gdn::NH + 1, t / n);
+  gdn::prep_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(pr), ldpr, n, static_cast<uint8_t*>(pool), page_bytes, tables,
       table_stride, conv_entry, conv_slot, conv_w, a_neg, dt_bias, reinterpret_cast<__nv_bfloat16*>(q),
       reinterpret_cast<__nv_bfloat16*>(k), reinterpret_cast<__nv_bfloat16*>(v), g,

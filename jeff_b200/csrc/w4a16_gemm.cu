@@ -489,6 +489,144 @@ __global__ void __launch_bounds__(128) lora_shrink_kernel(const __nv_bfloat16* _
   }
 }
 
+// ------------------------------------------------------------------ LoRA shrink, staged
+//
+// The same product for blocks of 64 rows that share one adapter (row_len a multiple of 64, K a multiple of 128):
+// 8 warps, warp w on rows 16 (w & 3) .. + 16 and on the K half w >> 2 of every 128-wide K step; the block's x rows and
+// its adapter's A rows for each K step are staged in shared memory by cp.async (double-buffered) and read by
+// ldmatrix. The two K halves' float32 partials are added in a fixed order: deterministic.
+constexpr int SH_ROWS = 64, SH_BK = 128, SH_PITCH = SH_BK + 8;   // 272-B rows: ldmatrix without bank conflicts
+
+__device__ __forceinline__ void sh_cp16(void* dst, const void* src, bool valid) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void sh_ldsm4(const void* p, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void sh_mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int NB>
+constexpr int shrink_staged_smem() {
+  return (2 * SH_ROWS * SH_PITCH + 2 * NB * 8 * SH_PITCH) * 2;
+}
+
+template <int NB>
+__global__ void __launch_bounds__(256) lora_shrink_staged_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
+                                                                 const __nv_bfloat16* __restrict__ A, int pool_rows,
+                                                                 const int* __restrict__ adapters, int row_len,
+                                                                 __nv_bfloat16* __restrict__ mid) {
+  constexpr int R = NB * 8;
+  extern __shared__ __align__(16) uint8_t sh_smem[];
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sh_smem);   // [2][64][SH_PITCH]
+  __nv_bfloat16* as = xs + 2 * SH_ROWS * SH_PITCH;                 // [2][R][SH_PITCH]
+  float* red = reinterpret_cast<float*>(sh_smem);                  // after the K loop: [64][R + 4]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rg = warp & 3, kh = warp >> 2;
+  const int m0 = blockIdx.x * SH_ROWS;
+  int a = adapters[m0 / row_len];
+  if (a < 0 || a >= pool_rows) a = 0;
+  const __nv_bfloat16* Aa = A + (size_t)a * R * K;
+  const int nk = K / SH_BK;
+
+  auto stage = [&](int kb, int buf) {
+    const int k0 = kb * SH_BK;
+    __nv_bfloat16* xd = xs + buf * SH_ROWS * SH_PITCH;
+    __nv_bfloat16* ad = as + buf * R * SH_PITCH;
+    for (int i = threadIdx.x; i < SH_ROWS * 16; i += 256) {
+      const int r = i >> 4, c = i & 15;
+      const bool valid = m0 + r < M;
+      sh_cp16(xd + r * SH_PITCH + c * 8, x + (size_t)(valid ? m0 + r : 0) * K + k0 + c * 8, valid);
+    }
+    for (int i = threadIdx.x; i < R * 16; i += 256) {
+      const int r = i >> 4, c = i & 15;
+      sh_cp16(ad + r * SH_PITCH + c * 8, Aa + (size_t)r * K + k0 + c * 8, true);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+
+  float acc[NB][4];
+#pragma unroll
+  for (int i = 0; i < NB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+  stage(0, 0);
+  for (int kb = 0; kb < nk; ++kb) {
+    if (kb + 1 < nk) {
+      stage(kb + 1, (kb + 1) & 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    const __nv_bfloat16* xb = xs + (kb & 1) * SH_ROWS * SH_PITCH;
+    const __nv_bfloat16* ab = as + (kb & 1) * R * SH_PITCH;
+#pragma unroll
+    for (int kk = 0; kk < 4; ++kk) {
+      const int kc = kh * 64 + kk * 16;
+      uint32_t af[4];
+      sh_ldsm4(xb + (rg * 16 + (lane & 15)) * SH_PITCH + kc + (lane >> 4) * 8, af);
+#pragma unroll
+      for (int nb = 0; nb < NB; nb += 2) {
+        const int i = lane >> 3;
+        uint32_t bfr[4];
+        sh_ldsm4(ab + (nb * 8 + (i >> 1) * 8 + (lane & 7)) * SH_PITCH + kc + (i & 1) * 8, bfr);
+        sh_mma(acc[nb], af, bfr[0], bfr[1]);
+        sh_mma(acc[nb + 1], af, bfr[2], bfr[3]);
+      }
+    }
+    __syncthreads();   // every warp is done with this buffer before the next stage() refills it
+  }
+  const int g = lane >> 2, t = lane & 3;
+  constexpr int RP = R + 4;
+  if (kh == 1) {
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const int col = nb * 8 + 2 * t;
+      red[(rg * 16 + g) * RP + col] = acc[nb][0];
+      red[(rg * 16 + g) * RP + col + 1] = acc[nb][1];
+      red[(rg * 16 + g + 8) * RP + col] = acc[nb][2];
+      red[(rg * 16 + g + 8) * RP + col + 1] = acc[nb][3];
+    }
+  }
+  __syncthreads();
+  if (kh == 0) {
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb) {
+      const int col = nb * 8 + 2 * t;
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const int row = rg * 16 + g + 8 * hf;
+        if (m0 + row < M) {
+          const float v0 = acc[nb][2 * hf] + red[row * RP + col];
+          const float v1 = acc[nb][2 * hf + 1] + red[row * RP + col + 1];
+          *reinterpret_cast<uint32_t*>(mid + (size_t)(m0 + row) * R + col) = pack_bf2(v0, v1);
+        }
+      }
+    }
+  }
+}
+
+template <int NB>
+int launch_shrink_staged(const __nv_bfloat16* x, int m, int k, const __nv_bfloat16* a, int pool_rows,
+                         const int* adapters, int row_len, __nv_bfloat16* mid, cudaStream_t st) {
+  constexpr int bytes = shrink_staged_smem<NB>();
+  static_assert(bytes <= 227 * 1024, "shared memory");
+  // set on every call: the attribute belongs to the current device
+  cudaError_t e = cudaFuncSetAttribute(lora_shrink_staged_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       bytes);
+  if (e != cudaSuccess) return status_of(e, "lora_shrink_staged_kernel: shared memory attribute");
+  lora_shrink_staged_kernel<NB><<<(m + SH_ROWS - 1) / SH_ROWS, 256, bytes, st>>>(x, m, k, a, pool_rows, adapters,
+                                                                                 row_len, mid);
+  return check_launch("lora_shrink_staged_kernel");
+}
+
 // ------------------------------------------------------------------ standalone dequantiser (verification)
 
 __global__ void int4_dequant_kernel(const int32_t* __restrict__ words, const __nv_bfloat16* __restrict__ scales,
@@ -568,6 +706,15 @@ extern "C" int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* l
   auto ab = reinterpret_cast<const __nv_bfloat16*>(lora_a);
   auto mb = reinterpret_cast<__nv_bfloat16*>(mid);
   cudaStream_t st = (cudaStream_t)stream;
+  if (row_len % w4::SH_ROWS == 0 && k % w4::SH_BK == 0) {
+    switch (rank) {
+      case 16: return w4::launch_shrink_staged<2>(xb, m, k, ab, pool_rows, adapters, row_len, mb, st);
+      case 32: return w4::launch_shrink_staged<4>(xb, m, k, ab, pool_rows, adapters, row_len, mb, st);
+      case 48: return w4::launch_shrink_staged<6>(xb, m, k, ab, pool_rows, adapters, row_len, mb, st);
+      case 64: return w4::launch_shrink_staged<8>(xb, m, k, ab, pool_rows, adapters, row_len, mb, st);
+      default: set_error("jb_lora_shrink: rank %d (16, 32, 48 or 64)", rank); return JB_EINVAL;
+    }
+  }
   switch (rank) {
     case 16: w4::lora_shrink_kernel<2><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
     case 32: w4::lora_shrink_kernel<4><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;

@@ -191,16 +191,28 @@ def test_int4_lora_product_swiglu_epilogue(fmt: str) -> None:
     torch.testing.assert_close(got, want, rtol=4 * BF16_STEP, atol=5e-4)
 
 
-def test_lora_shrink_matches_the_oracle() -> None:
-    g = torch.Generator().manual_seed(3)
-    m, k, rank = 256, 1024, 48
+@pytest.mark.parametrize(("m", "k", "rank", "row_len"), [
+    (256, 1024, 48, 64),      # staged kernel (64-row blocks of one adapter)
+    (512, 3584, 16, 128),     # staged, K = 3584
+    (208, 2048, 64, 64),      # staged, m not a multiple of the 64-row block
+    (384, 1024, 32, 128),     # staged
+    (256, 1024, 48, 32),      # 16-row kernel: rows of 32 tokens
+    (96, 960, 16, 32),        # 16-row kernel: K not a multiple of 128
+])
+def test_lora_shrink_matches_the_oracle(m: int, k: int, rank: int, row_len: int) -> None:
+    """mid = bf16(x A[a]^T) per row's adapter: within one bf16 step of the float32 product (summation order), and the
+    same bits on a second call (fixed-order reductions)."""
+    g = torch.Generator().manual_seed(m + k + rank)
     x = torch.randn(m, k, generator=g).to(torch.bfloat16)
     a_pool = (torch.randn(3, rank, k, generator=g) * 0.02).to(torch.bfloat16)
-    adapters = torch.tensor([2, 0, 1, 2], dtype=torch.int32)
-    got = kernels.lora_shrink(x.cuda(), a_pool.cuda(), adapters.cuda(), 64).cpu().float()
-    row_of = adapters.long().repeat_interleave(64)
+    rows = (m + row_len - 1) // row_len
+    adapters = torch.randint(0, 3, (rows,), generator=g, dtype=torch.int32)
+    got = kernels.lora_shrink(x.cuda(), a_pool.cuda(), adapters.cuda(), row_len).cpu()
+    row_of = adapters.long().repeat_interleave(row_len)[:m]
     want = torch.stack([x[i].float() @ a_pool[row_of[i]].float().T for i in range(m)])
-    torch.testing.assert_close(got, bf(want), rtol=BF16_STEP, atol=1e-6)
+    torch.testing.assert_close(got.float(), bf(want), rtol=BF16_STEP, atol=1e-6)
+    again = kernels.lora_shrink(x.cuda(), a_pool.cuda(), adapters.cuda(), row_len).cpu()
+    assert torch.equal(got, again)
 
 
 # ---------------------------------------------------------------- norms and activations
@@ -265,7 +277,7 @@ def test_readout_rows_match_the_oracle(b: int) -> None:
 
 
 @pytest.mark.parametrize("b", BATCHES)
-@pytest.mark.parametrize("n", [32, 64])
+@pytest.mark.parametrize("n", [32, 64, 160])
 @pytest.mark.parametrize("gdn_layer", [0, 13, 17])
 def test_gdn_prep_rows_match_the_oracle(pool_fixture, b: int, n: int, gdn_layer: int) -> None:
     """q, k within two bf16 steps (the L2 norm's sum order), v and beta within one, g float32 within 1e-5."""
@@ -287,6 +299,43 @@ def test_gdn_prep_rows_match_the_oracle(pool_fixture, b: int, n: int, gdn_layer:
             torch.testing.assert_close(x[r].cpu().float(), y, rtol=rtol, atol=1e-6, msg=lambda m, nm=name: f"{nm}: {m}")
         torch.testing.assert_close(got[3][r].cpu(), want[3], rtol=1e-5, atol=1e-6)
         torch.testing.assert_close(got[4][r].cpu().float(), want[4], rtol=BF16_STEP, atol=1e-6)
+
+
+def test_gdn_prep_rows_prefix_mode_masks_padding_and_writes_conv_tails(pool_fixture) -> None:
+    """The prefix pass's prep: tokens at or past a row's real length get g = beta = 0 (q, k, v as usual), and each
+    row's last three real convolution inputs (from the cached tail when the row is shorter than three) go to its
+    output pages, bit for bit."""
+    pool, slots, states = pool_fixture
+    ss = [slots[45], 0, slots[1000]]
+    tables, _ = tables_for(pool, ss)
+    b, n, gdn_layer = 3, 96, 5
+    real = torch.tensor([96, 2, 57], dtype=torch.int32)
+    g = torch.Generator().manual_seed(55)
+    conv_w = bf(0.5 * torch.randn(4, C.QKV_DIM, generator=g)).contiguous()
+    a_log = torch.randn(C.NV, generator=g)
+    dt_bias = torch.randn(C.NV, generator=g)
+    pr = torch.randn(b * n, C.GDN_PROJ, generator=g).to(torch.bfloat16)
+    fresh = [pool.reserve(7, f"prep tail {i}", 64) for i in range(b)]
+    pool.pin(fresh)
+    try:
+        out_tables, _ = tables_for(pool, fresh)
+        got = kernels.gdn_prep_rows(pr.cuda(), pool, tables, gdn_layer, conv_w.cuda(), (-torch.exp(a_log)).cuda(),
+                                    dt_bias.cuda(), n, real=real.cuda(), out_tables=out_tables)
+        torch.cuda.synchronize()
+        for r in range(b):
+            rl = int(real[r])
+            tail = states[ss[r]][0][gdn_layer]
+            want = model_ref.gdn_prep(pr[r * n:(r + 1) * n], tail, conv_w.T, a_log, dt_bias)
+            torch.testing.assert_close(got[2][r].cpu().float(), want[2], rtol=BF16_STEP, atol=1e-6)
+            torch.testing.assert_close(got[3][r, :rl].cpu(), want[3][:rl], rtol=1e-5, atol=1e-6)
+            assert not got[3][r, rl:].any() and not got[4][r, rl:].float().any()
+            inputs = torch.cat([tail.to(torch.bfloat16), pr[r * n:(r + 1) * n, :C.QKV_DIM]])
+            conv_out = pool.gather(fresh[r])[0][gdn_layer].cpu()
+            assert torch.equal(conv_out, inputs[rl:rl + 3]), f"row {r}: conv tail"
+    finally:
+        pool.unpin(fresh)
+        for slot in fresh:
+            pool.release(slot)
 
 
 GDN_RTOL, GDN_ATOL = 2.0 ** -6, 2.0 ** -9
