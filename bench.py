@@ -92,37 +92,21 @@ class Clocks:
 
 
 def dist_setup(gpus: int) -> tuple[int, int, int]:
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world > 1:
-        import datetime
+    from jeff_b200 import replicas
 
-        import torch.distributed as dist
-
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
-                                device_id=torch.device("cuda", local))
-    elif torch.cuda.is_available():
-        torch.cuda.set_device(0)
-    return rank, world, local
+    return replicas.setup("nccl", timeout_s=600)
 
 
 def barrier(world: int) -> None:
-    if world > 1:
-        import torch.distributed as dist
+    from jeff_b200 import replicas
 
-        dist.barrier()
+    replicas.barrier(world)
 
 
 def max_over_ranks(value: float, world: int) -> float:
-    if world == 1:
-        return value
-    import torch.distributed as dist
+    from jeff_b200 import replicas
 
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    return float(t.item())
+    return replicas.max_over_ranks(value, world, device="cuda")
 
 
 # ---------------------------------------------------------------- the CPU baseline (oracle port of the standard path)
@@ -198,10 +182,9 @@ def build_replica(rank: int, world: int):
     for ad in adapters:
         fast.add_adapter(ad)
     if world > 1:
-        import torch.distributed as dist
+        from jeff_b200 import replicas
 
-        for t in fast.tensors():
-            dist.broadcast(t, 0)
+        replicas.broadcast_tensors(fast.tensors(), 0)
         torch.cuda.synchronize()
     return model, adapters, fast
 

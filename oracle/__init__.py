@@ -9,7 +9,7 @@ imports, calls or links anything here, and has no CPU fallback.
 - model_ref: torch-CPU restatement of every kernel of the pass and of the whole batched forward, with the fast path's
   bfloat16 rounding points (or none, `exact=True`, to compare with the reference's float32 standard path).
 
-Pinning: tests/golden/ holds vectors produced by running the reference's own code in a container where
-/root/reference exists (tests/golden/make_golden.py): its int4 packer/dequantiser, its PrefixShapes layout, the
+Pinning: tests/golden/ holds vectors produced by running the reference's own code on a machine with a checkout of
+the reference (tests/golden/make_golden.py, pointed at it by $JEFF_REFERENCE): its int4 packer/dequantiser, its PrefixShapes layout, the
 transformers torch_chunk_gated_delta_rule (the standard path's scan) and the transformers Qwen3.5 text model forward
 on seeded synthetic weights. tests/test_oracle_golden.py checks this oracle against them."""

@@ -1,9 +1,9 @@
 """Generate the golden vectors under tests/golden/ by running the REFERENCE's own code (firelex/jeff and the
-transformers Qwen3.5 model its standard path runs). Needs the reference checkout (default /root/reference, or
-$JEFF_REFERENCE) and is run by hand on a machine that has it; the fixtures it writes are committed, and nothing at
-test time reads the reference.
+transformers Qwen3.5 model its standard path runs). Needs a checkout of the reference, named by $JEFF_REFERENCE,
+and is run by hand on a machine that has one; the fixtures it writes are committed, and nothing at test time reads
+the reference.
 
-    python tests/golden/make_golden.py
+    JEFF_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 Writes:
 - int4_golden.npz: the reference's pack_int4, pack_kernel (words, scales), dequantize and round_to_nearest on seeded
@@ -31,7 +31,9 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parent.parent
-REF = Path(os.environ.get("JEFF_REFERENCE", "/root/reference"))
+if "JEFF_REFERENCE" not in os.environ:
+    sys.exit("make_golden.py: set JEFF_REFERENCE to a checkout of the reference")
+REF = Path(os.environ["JEFF_REFERENCE"])
 sys.path[:0] = [str(ROOT), str(REF / "runtime/python/src"), str(REF / "packages/python/src")]
 
 from jeff_runtime.engine import int4 as ref_int4  # noqa: E402
