@@ -1,8 +1,9 @@
 """B200Engine end to end on a B200: prepare, predict_many over groups of two adapters and the base (prefix passes
 for new prefixes, cached prefixes on the second call, decision passes), against the CPU oracle of the same rows
-(prefix pass, then the decision pass from the prefix's state). A 4-layer synthetic model, so the chain is short
-enough for the probabilities to be held to 1e-2; decisions and abstentions (threshold 0.8) must agree except at a
-near-tie."""
+(prefix pass, then the decision pass from the prefix's state). A 4-layer synthetic model run as two chained passes
+(the prefix pass's states feed the decision pass), so bf16 summation-order drift accumulates over eight layer
+applications: probabilities are held to 2e-2 here (the teacher-forced tests of test_forward_gpu.py hold the 1e-2
+bar), and decisions and abstentions (threshold 0.8) must agree except at a near-tie."""
 
 from __future__ import annotations
 
@@ -16,6 +17,7 @@ from oracle import model_ref
 pytestmark = pytest.mark.gpu
 
 VOCAB = 4096
+PROB_TOL = 2e-2
 
 
 @pytest.fixture(scope="module")
@@ -72,7 +74,7 @@ def test_engine_groups_match_the_oracle(setup) -> None:
             for row, got, tokens in zip(rows, result.probabilities, result.input_tokens, strict=True):
                 want = oracle_probs(model, adapter, texts, row)
                 diff = float((torch.tensor(got) - want).abs().max())
-                assert diff < 1e-2, f"{adapter_id}: |p - p_oracle| = {diff}"
+                assert diff < PROB_TOL, f"{adapter_id}: |p - p_oracle| = {diff}"
                 assert tokens == len(texts[row["prefix_text"]]) + len(row["new_ids"])
                 mine, theirs = make_decision(got, 0.8), make_decision(want.tolist(), 0.8)
                 top2 = sorted(want.tolist())[-2:] if len(want) > 1 else [0.0, 1.0]
