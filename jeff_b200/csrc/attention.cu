@@ -32,6 +32,14 @@ __global__ void __launch_bounds__(384) prep_kernel(const __nv_bfloat16* __restri
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = t / n;
   const __nv_bfloat16* src = pr + (size_t)t * ldpr;
+  // the token's 32 rotary angles, shared by every query and key head: cos and sin rounded to bf16 once
+  __shared__ float rc[ROT / 2], rsn[ROT / 2];
+  if (threadIdx.x < ROT / 2) {
+    const float f = (float)(pos[row] + (t - row * n)) * inv_freq[threadIdx.x];
+    rc[threadIdx.x] = round_bf(cosf(f));
+    rsn[threadIdx.x] = round_bf(sinf(f));
+  }
+  __syncthreads();
   if (w >= NQ + NKV) {
     const int hh = w - NQ - NKV;
     const uint4 val = reinterpret_cast<const uint4*>(src + NQ * 2 * HD + NKV * HD + hh * HD)[lane];
@@ -57,12 +65,10 @@ __global__ void __launch_bounds__(384) prep_kernel(const __nv_bfloat16* __restri
   for (int e = 0; e < 8; ++e) part[e] = __shfl_xor_sync(0xffffffffu, y[e], 4);
   float out[8];
   if (lane < ROT / 8) {
-    const float p = (float)(pos[row] + (t - row * n));
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       const int d = lane * 8 + e;
-      const float f = p * inv_freq[d % (ROT / 2)];
-      const float c = round_bf(cosf(f)), s = round_bf(sinf(f));
+      const float c = rc[d % (ROT / 2)], s = rsn[d % (ROT / 2)];
       const float rot = d < ROT / 2 ? -part[e] : part[e];
       out[e] = round_bf(y[e] * c) + round_bf(rot * s);
     }

@@ -176,31 +176,36 @@ __global__ void gate_mul_kernel(const __nv_bfloat16* __restrict__ o, const __nv_
   reinterpret_cast<uint4*>(y + r * 2048)[c] = pack8(out);
 }
 
-// one warp per (token, head of 128): y = bf16(bf16(w * bf16(rms(o))) * silu(z))
+// one half-warp per (token, head of 128), 8 channels per lane: y = bf16(bf16(w * bf16(rms(o))) * silu(z))
 __global__ void gated_norm_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ pr, int ldpr,
                                   int z_off, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                   int rows) {
-  const size_t wid = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (wid >= (size_t)rows * 16) return;
-  const size_t r = wid / 16;
-  const int h = (int)(wid % 16);
-  const uint2 ou = reinterpret_cast<const uint2*>(o + (r * 16 + h) * 128)[lane];
-  float v[4] = {bf_lo(ou.x), bf_hi(ou.x), bf_lo(ou.y), bf_hi(ou.y)};
-  const float ss = warp_sum(v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3]);
-  const float rs = rsqrtf(ss / 128.f + EPS);
-  const uint2 zu = reinterpret_cast<const uint2*>(pr + r * ldpr + z_off + h * 128)[lane];
-  const uint2 wu = reinterpret_cast<const uint2*>(w)[lane];
-  const float z[4] = {bf_lo(zu.x), bf_hi(zu.x), bf_lo(zu.y), bf_hi(zu.y)};
-  const float wv[4] = {bf_lo(wu.x), bf_hi(wu.x), bf_lo(wu.y), bf_hi(wu.y)};
-  float out[4];
+  const size_t pair = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;   // (token, head) index
+  const int sub = threadIdx.x & 15;
+  const bool live = pair < (size_t)rows * 16;
+  const size_t r = live ? pair / 16 : 0;
+  const int h = live ? (int)(pair % 16) : 0;
+  float v[8], z[8], wv[8];
+  unpack8(reinterpret_cast<const uint4*>(o + (r * 16 + h) * 128)[sub], v);
+  float ss = 0.f;
 #pragma unroll
-  for (int e = 0; e < 4; ++e) {
+  for (int e = 0; e < 8; ++e) ss += v[e] * v[e];
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  const float rs = rsqrtf(ss / 128.f + EPS);
+  unpack8(reinterpret_cast<const uint4*>(pr + r * ldpr + z_off + h * 128)[sub], z);
+  unpack8(reinterpret_cast<const uint4*>(w)[sub], wv);
+  float out[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
     const float nv = round_bf(v[e] * rs);
     const float gw = round_bf(wv[e] * nv);
     out[e] = gw * (z[e] / (1.0f + expf(-z[e])));
   }
-  reinterpret_cast<uint2*>(y + r * 2048 + h * 128)[lane] = make_uint2(pack_bf2(out[0], out[1]), pack_bf2(out[2], out[3]));
+  if (live)
+    reinterpret_cast<uint4*>(y + r * 2048 + h * 128)[sub] =
+        make_uint4(pack_bf2(out[0], out[1]), pack_bf2(out[2], out[3]), pack_bf2(out[4], out[5]),
+                   pack_bf2(out[6], out[7]));
 }
 
 // one block of 256 threads per row: 255 logits = bf16(W[a] . h) (fp32 sums), mask, temperature, softmax
@@ -305,10 +310,13 @@ extern "C" int jb_gate_mul(const uint16_t* o, const uint16_t* pr, int ldpr, uint
 extern "C" int jb_gated_norm(const uint16_t* o, const uint16_t* pr, int ldpr, int z_off, const uint16_t* w,
                              uint16_t* y, int rows, void* stream) {
   JB_REQUIRE(o && pr && w && y, "jb_gated_norm: null pointer");
-  JB_REQUIRE(rows > 0 && z_off >= 0 && z_off % 8 == 0 && ldpr >= z_off + 2048 && ldpr % 4 == 0,
-             "jb_gated_norm: rows %d, ldpr %d, z_off %d", rows, ldpr, z_off);
-  const size_t warps = (size_t)rows * 16;
-  ew::gated_norm_kernel<<<blocks_for(warps * 32, 256), 256, 0, (cudaStream_t)stream>>>(
+  JB_REQUIRE(rows > 0 && z_off >= 0 && z_off % 8 == 0 && ldpr >= z_off + 2048 && ldpr % 8 == 0,
+             "jb_gated_norm: rows %d, ldpr %d, z_off %d (multiples of 8)", rows, ldpr, z_off);
+  JB_REQUIRE(((reinterpret_cast<uintptr_t>(o) | reinterpret_cast<uintptr_t>(pr) | reinterpret_cast<uintptr_t>(w) |
+               reinterpret_cast<uintptr_t>(y)) & 15) == 0,
+             "jb_gated_norm: o, pr, w and y must be 16-byte aligned");
+  const size_t threads = (size_t)rows * 16 * 16;   // 16 per (token, head)
+  ew::gated_norm_kernel<<<blocks_for(threads, 256), 256, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(pr), ldpr, z_off,
       reinterpret_cast<const __nv_bfloat16*>(w), reinterpret_cast<__nv_bfloat16*>(y), rows);
   return check_launch("gated_norm_kernel");

@@ -33,6 +33,8 @@ struct Smem {
   __nv_bfloat16 ts[C * P64];    // T (bf16)
   __nv_bfloat16 ps[C * P64];    // Q K^T ∘ Γ, causal (bf16)
   float gc[C];
+  float eg[C];                  // e^gc per token
+  float ed[C];                  // e^{gc_last - gc} per token
   float beta[C];
 };
 
@@ -159,6 +161,10 @@ __global__ void __launch_bounds__(256, 1) chunk_kernel(const __nv_bfloat16* __re
     }
     __syncthreads();
     const float glast = sm.gc[C - 1];
+    if (threadIdx.x < C) {
+      sm.eg[threadIdx.x] = expf(sm.gc[threadIdx.x]);
+      sm.ed[threadIdx.x] = expf(glast - sm.gc[threadIdx.x]);
+    }
 
     // ---- KK^T and QK^T (64 x 64): warp (wr, wc) rows 16 wr, cols 32 wc
     {
@@ -197,7 +203,7 @@ __global__ void __launch_bounds__(256, 1) chunk_kernel(const __nv_bfloat16* __re
     // ---- scaled operand copies (the raw K and V are no longer needed after this)
     for (int i = threadIdx.x; i < C * D / 2; i += 256) {
       const int t = i / (D / 2), d = (i % (D / 2)) * 2;
-      const float eg = expf(sm.gc[t]), bt = sm.beta[t], ed = expf(glast - sm.gc[t]);
+      const float eg = sm.eg[t], bt = sm.beta[t], ed = sm.ed[t];
       const float k0 = __bfloat162float(sm.ks[t * P16 + d]), k1 = __bfloat162float(sm.ks[t * P16 + d + 1]);
       const float q0 = __bfloat162float(sm.qs[t * P16 + d]), q1 = __bfloat162float(sm.qs[t * P16 + d + 1]);
       const float v0 = __bfloat162float(sm.vs[t * P16 + d]), v1 = __bfloat162float(sm.vs[t * P16 + d + 1]);
@@ -227,28 +233,31 @@ __global__ void __launch_bounds__(256, 1) chunk_kernel(const __nv_bfloat16* __re
       for (int i = 0; i < 16; ++i) sm.tf[(base + i) * PF + base + j] = col[i];
     }
     __syncthreads();
-    // off-diagonal blocks, block row r = 1..3, in dependency order: T_rc = D_r (sum_{m=c}^{r-1} A_rm T_mc)
+    // off-diagonal blocks T_rc = T_rr (sum_{m=c}^{r-1} A_rm T_mc), by distance d = r - c from the diagonal: the
+    // blocks of one distance need only blocks nearer the diagonal, so each distance is one parallel step
     {
       const int i = threadIdx.x >> 4, j = threadIdx.x & 15;   // element of a 16 x 16 block
-      for (int r = 1; r < 4; ++r) {
-        for (int cc = r - 1; cc >= 0; --cc) {
-          // tmp = sum_m A_rm T_mc   (m from cc to r-1)
+      for (int d = 1; d < 4; ++d) {
+        for (int c = 0; c + d < 4; ++c) {
+          const int r = c + d;
           float tmp = 0.f;
-          for (int m = cc; m < r; ++m)
+          for (int m = c; m < r; ++m)
 #pragma unroll
             for (int kx = 0; kx < 16; ++kx)
-              tmp += sm.amat[(16 * r + i) * PF + 16 * m + kx] * sm.tf[(16 * m + kx) * PF + 16 * cc + j];
-          // stage tmp in the (r, cc) block of amat's upper triangle mirror: use ts-free fp32 scratch in amat (row
-          // block cc, col block r) which is zero-structured (strictly upper) and unused
-          sm.amat[(16 * cc + i) * PF + 16 * r + j] = tmp;
-          __syncthreads();
+              tmp += sm.amat[(16 * r + i) * PF + 16 * m + kx] * sm.tf[(16 * m + kx) * PF + 16 * c + j];
+          // staged in block (c, r) of amat's strictly upper part, which holds nothing
+          sm.amat[(16 * c + i) * PF + 16 * r + j] = tmp;
+        }
+        __syncthreads();
+        for (int c = 0; c + d < 4; ++c) {
+          const int r = c + d;
           float acc = 0.f;
 #pragma unroll
           for (int kx = 0; kx < 16; ++kx)
-            acc += sm.tf[(16 * r + i) * PF + 16 * r + kx] * sm.amat[(16 * cc + kx) * PF + 16 * r + j];
-          sm.tf[(16 * r + i) * PF + 16 * cc + j] = acc;
-          __syncthreads();
+            acc += sm.tf[(16 * r + i) * PF + 16 * r + kx] * sm.amat[(16 * c + kx) * PF + 16 * r + j];
+          sm.tf[(16 * r + i) * PF + 16 * c + j] = acc;
         }
+        __syncthreads();
       }
     }
     // T (bf16), zero above the diagonal
