@@ -102,7 +102,8 @@ __global__ void __launch_bounds__(128) prep_kernel(const __nv_bfloat16* __restri
       acc += w[1][e] * x1[e];
       acc += w[2][e] * x2[e];
       acc += w[3][e] * x3[e];
-      c[e] = round_bf(acc / (1.0f + expf(-acc)));
+      // SiLU with the fast intrinsics (the result is rounded to bf16 at once; __fdividef(x, inf) = 0 is the limit)
+      c[e] = round_bf(__fdividef(acc, 1.0f + __expf(-acc)));
       x0[e] = x1[e];
       x1[e] = x2[e];
       x2[e] = x3[e];
