@@ -15,6 +15,8 @@ constexpr int BQ = 16;                 // new tokens per CTA
 constexpr int BKN = 32;                // keys per tile
 constexpr int PITCH = HD * 2 + 16;     // bytes per key row in shared memory (16 B pad: conflict-free)
 constexpr int TILE_BYTES = BKN * PITCH;
+constexpr int XCH_BYTES = 8 * 32 * 16 * 4;   // per warp, its partial S (16 x 32 fp32) for the warp sharing its head
+constexpr int ATTN_SMEM = 4 * TILE_BYTES + XCH_BYTES;
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -98,6 +100,11 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
@@ -130,20 +137,22 @@ __global__ void __launch_bounds__(256, 1) paged_attention_kernel(
   const int64_t layer_off = (int64_t)attn_layer * 2 * PAGE * NKV * HD * 2;
   const int64_t kv_half = (int64_t)PAGE * NKV * HD * 2;   // K block -> V block of one layer
 
-  // Q fragments: rows = tokens qb*16 + gr (+8), k = head dims
-  uint32_t qf[16][4];
+  // Q fragments of this warp's half of the head dims [dim0, dim0 + 128): rows = tokens qb*16 + gr (+8). The warp
+  // w ^ 4 holds the other half of the same head: each computes its half of Q K^T and they add the halves.
+  uint32_t qf[8][4];
   {
     const size_t t0 = (size_t)row * n + qb * BQ + gr;
-    const __nv_bfloat16* q0 = q + (t0 * NQ + head) * HD;
-    const __nv_bfloat16* q1 = q + ((t0 + 8) * NQ + head) * HD;
+    const __nv_bfloat16* q0 = q + (t0 * NQ + head) * HD + dim0;
+    const __nv_bfloat16* q1 = q + ((t0 + 8) * NQ + head) * HD + dim0;
 #pragma unroll
-    for (int kk = 0; kk < 16; ++kk) {
+    for (int kk = 0; kk < 8; ++kk) {
       qf[kk][0] = *reinterpret_cast<const uint32_t*>(q0 + kk * 16 + 2 * tq);
       qf[kk][1] = *reinterpret_cast<const uint32_t*>(q1 + kk * 16 + 2 * tq);
       qf[kk][2] = *reinterpret_cast<const uint32_t*>(q0 + kk * 16 + 8 + 2 * tq);
       qf[kk][3] = *reinterpret_cast<const uint32_t*>(q1 + kk * 16 + 8 + 2 * tq);
     }
   }
+  float* xch = reinterpret_cast<float*>(sm + 4 * TILE_BYTES);   // [warp][16 values][32 lanes]
   float o[16][4];
 #pragma unroll
   for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
@@ -190,19 +199,31 @@ __global__ void __launch_bounds__(256, 1) paged_attention_kernel(
     __syncthreads();
     const uint8_t* ks = sm + buf * 2 * TILE_BYTES;
     const uint8_t* vs = ks + TILE_BYTES;
-    // S = Q K^T: 16 rows x 32 keys
+    // S = Q K^T: 16 rows x 32 keys, this warp's 128 dims (K fragments by ldmatrix: keys as rows), then the
+    // partner's partial added (a + b = b + a: both warps hold the same S)
     float s[4][4];
 #pragma unroll
     for (int nb = 0; nb < 4; ++nb) {
       s[nb][0] = s[nb][1] = s[nb][2] = s[nb][3] = 0.f;
-      const uint8_t* krow = ks + (nb * 8 + gr) * PITCH;
+      const int mi = lane >> 3;
+      const uint8_t* krow = ks + (nb * 8 + (lane & 7)) * PITCH + dim0 * 2 + (mi & 1) * 16 + (mi >> 1) * 32;
 #pragma unroll
-      for (int kk = 0; kk < 16; ++kk) {
-        const uint32_t b0 = *reinterpret_cast<const uint32_t*>(krow + (kk * 16 + 2 * tq) * 2);
-        const uint32_t b1 = *reinterpret_cast<const uint32_t*>(krow + (kk * 16 + 8 + 2 * tq) * 2);
+      for (int kk = 0; kk < 8; kk += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(smem_u32(krow + kk * 32), b0, b1, b2, b3);
         mma16816(s[nb], qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3], b0, b1);
+        mma16816(s[nb], qf[kk + 1][0], qf[kk + 1][1], qf[kk + 1][2], qf[kk + 1][3], b2, b3);
       }
     }
+#pragma unroll
+    for (int nb = 0; nb < 4; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) xch[(warp * 16 + nb * 4 + e) * 32 + lane] = s[nb][e];
+    named_barrier(1 + (warp & 3), 64);   // the two warps of this head
+#pragma unroll
+    for (int nb = 0; nb < 4; ++nb)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) s[nb][e] += xch[((warp ^ 4) * 16 + nb * 4 + e) * 32 + lane];
     // masks and the online softmax (rows gr and gr + 8 of this warp)
     const int tok0 = qb * BQ + gr, tok1 = tok0 + 8;
     float mx0 = m0, mx1 = m1;
@@ -335,7 +356,7 @@ extern "C" int jb_paged_attention(const uint16_t* q, const void* pool, int64_t p
              "jb_paged_attention: attention layer %d of %d does not fit pages of %lld bytes", attn_layer, attn_layers,
              (long long)page_bytes);
   JB_REQUIRE(kv_entry >= 0 && kv_entry <= table_stride, "jb_paged_attention: kv_entry %d", kv_entry);
-  constexpr int SMEM = 4 * attn::TILE_BYTES;
+  constexpr int SMEM = attn::ATTN_SMEM;
   static bool configured[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);

@@ -90,31 +90,40 @@ __global__ void __launch_bounds__(128) prep_kernel(const __nv_bfloat16* __restri
     load4(p2 < 0 ? tail + (size_t)(p2 + 3) * QKV + ch : pr + (rbase + p2) * ldpr + ch, x2);
   }
   __nv_bfloat16* dst = part == 0 ? q : (part == 1 ? k : v);
-#pragma unroll 4
-  for (int tt = t0; tt < t1; ++tt) {
-    float x3[4];
-    load4(pr + (rbase + tt) * ldpr + ch, x3);
-    float c[4];
+  // tokens in groups of 8: the group's 8 loads are issued before any of them is used
+  for (int tb = t0; tb < t1; tb += 8) {
+    uint2 raw[8];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      float acc = 0.f;
-      acc += w[0][e] * x0[e];
-      acc += w[1][e] * x1[e];
-      acc += w[2][e] * x2[e];
-      acc += w[3][e] * x3[e];
-      // SiLU with the fast intrinsics (the result is rounded to bf16 at once; __fdividef(x, inf) = 0 is the limit)
-      c[e] = round_bf(__fdividef(acc, 1.0f + __expf(-acc)));
-      x0[e] = x1[e];
-      x1[e] = x2[e];
-      x2[e] = x3[e];
-    }
-    const size_t o = ((rbase + tt) * NH + head) * HDIM + lane * 4;
-    if (part < 2) {
-      const float ss = warp_sum(c[0] * c[0] + c[1] * c[1] + c[2] * c[2] + c[3] * c[3]);
-      const float rs = rsqrtf(ss + 1e-6f);
-      *reinterpret_cast<uint2*>(dst + o) = make_uint2(pack_bf2(c[0] * rs, c[1] * rs), pack_bf2(c[2] * rs, c[3] * rs));
-    } else {
-      *reinterpret_cast<uint2*>(dst + o) = make_uint2(pack_bf2(c[0], c[1]), pack_bf2(c[2], c[3]));
+    for (int u = 0; u < 8; ++u)
+      raw[u] = *reinterpret_cast<const uint2*>(pr + (rbase + min(tb + u, t1 - 1)) * ldpr + ch);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int tt = tb + u;
+      if (tt >= t1) break;   // the same for the whole warp
+      const float x3[4] = {bf_lo(raw[u].x), bf_hi(raw[u].x), bf_lo(raw[u].y), bf_hi(raw[u].y)};
+      float c[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float acc = 0.f;
+        acc += w[0][e] * x0[e];
+        acc += w[1][e] * x1[e];
+        acc += w[2][e] * x2[e];
+        acc += w[3][e] * x3[e];
+        // SiLU with the fast intrinsics (the result is rounded to bf16 at once; __fdividef(x, inf) = 0 is the limit)
+        c[e] = round_bf(__fdividef(acc, 1.0f + __expf(-acc)));
+        x0[e] = x1[e];
+        x1[e] = x2[e];
+        x2[e] = x3[e];
+      }
+      const size_t o = ((rbase + tt) * NH + head) * HDIM + lane * 4;
+      if (part < 2) {
+        const float ss = warp_sum(c[0] * c[0] + c[1] * c[1] + c[2] * c[2] + c[3] * c[3]);
+        const float rs = rsqrtf(ss + 1e-6f);
+        *reinterpret_cast<uint2*>(dst + o) =
+            make_uint2(pack_bf2(c[0] * rs, c[1] * rs), pack_bf2(c[2] * rs, c[3] * rs));
+      } else {
+        *reinterpret_cast<uint2*>(dst + o) = make_uint2(pack_bf2(c[0], c[1]), pack_bf2(c[2], c[3]));
+      }
     }
   }
   if (real && out_tables && t0 == 0) {
