@@ -51,29 +51,53 @@ def peaks() -> dict:
 
 
 class Clocks:
-    """nvidia-smi samples of SM clock and throttle reasons while the timed region runs."""
+    """SM clock and throttle reasons sampled while the timed regions run: NVML every 20 ms (read-only queries), or
+    nvidia-smi when NVML is not available."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
 
     def __init__(self, index: int) -> None:
         self.index = index
         self.samples: list[tuple[float, float, str]] = []
         self._stop = threading.Event()
         self._thread = threading.Thread(target=self._run, daemon=True)
+        self._nvml = None
+        try:
+            import pynvml
 
-    def _run(self) -> None:
+            pynvml.nvmlInit()
+            uuid = str(torch.cuda.get_device_properties(index).uuid)
+            handle = pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            self._nvml = (pynvml, handle)
+        except Exception:
+            self._nvml = None
+
+    def _sample_nvml(self) -> None:
+        nv, h = self._nvml
+        sm = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+        mx = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        bits = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+        active = [n for n, b in self.REASONS.items() if bits & b]
+        self.samples.append((float(sm), float(mx), ",".join(active)))
+
+    def _sample_smi(self) -> None:
         q = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}", "--format=csv,noheader,nounits"],
+                             capture_output=True, text=True, timeout=5)
+        parts = [p.strip() for p in out.stdout.strip().split(",")]
+        if len(parts) == 6:
+            active = [n for n, v in zip(self.REASONS, parts[2:]) if v.lower() == "active"]
+            self.samples.append((float(parts[0]), float(parts[1]), ",".join(active)))
+
+    def _run(self) -> None:
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={q}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
-                parts = [p.strip() for p in out.stdout.strip().split(",")]
-                if len(parts) == 6:
-                    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-                    active = [n for n, v in zip(names, parts[2:]) if v.lower() == "active"]
-                    self.samples.append((float(parts[0]), float(parts[1]), ",".join(active)))
+                self._sample_nvml() if self._nvml is not None else self._sample_smi()
             except Exception:
-                pass
-            self._stop.wait(0.2)
+                if self._nvml is not None:
+                    self._nvml = None
+            self._stop.wait(0.02 if self._nvml is not None else 0.2)
 
     def __enter__(self) -> "Clocks":
         self._thread.start()

@@ -91,6 +91,51 @@ __global__ void __launch_bounds__(128) add_rms_kernel(const __nv_bfloat16* __res
   }
 }
 
+// the same for rows of 1024: one warp per row (4 x 16 bytes per lane), 4 rows per block, no block barriers
+__global__ void __launch_bounds__(128) add_rms_1024_kernel(const __nv_bfloat16* __restrict__ x,
+                                                           const __nv_bfloat16* __restrict__ d,
+                                                           const float* __restrict__ w1, __nv_bfloat16* xo,
+                                                           __nv_bfloat16* __restrict__ h, int rows) {
+  constexpr int N = 1024;
+  const int lane = threadIdx.x & 31;
+  const size_t row = (size_t)blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (row >= (size_t)rows) return;
+  float v[4][8];
+  uint4 xu[4], du[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) xu[j] = reinterpret_cast<const uint4*>(x + row * N)[lane + 32 * j];
+  if (d) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) du[j] = reinterpret_cast<const uint4*>(d + row * N)[lane + 32 * j];
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    unpack8(xu[j], v[j]);
+    if (d) {
+      float dv[8];
+      unpack8(du[j], dv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) v[j][e] = round_bf(v[j][e] + dv[e]);
+      reinterpret_cast<uint4*>(xo + row * N)[lane + 32 * j] = pack8(v[j]);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) ss += v[j][e] * v[j][e];
+  }
+  const float rs = rsqrtf(warp_sum(ss) / N + EPS);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = lane + 32 * j;
+    const float4 wa = reinterpret_cast<const float4*>(w1)[2 * c];
+    const float4 wb = reinterpret_cast<const float4*>(w1)[2 * c + 1];
+    const float w[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    float o[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) o[e] = v[j][e] * rs * w[e];
+    reinterpret_cast<uint4*>(h + row * N)[c] = pack8(o);
+  }
+}
+
 // hidden[b] = bf16(rms(bf16(x[t] + d[t])) * w1), t = b * row_len + last[b]
 __global__ void __launch_bounds__(128) rms_last_kernel(const __nv_bfloat16* __restrict__ x,
                                                        const __nv_bfloat16* __restrict__ d,
@@ -260,6 +305,12 @@ extern "C" int jb_add_rms(const uint16_t* x, const uint16_t* d, const float* w1,
   JB_REQUIRE(x && w1 && h, "jb_add_rms: null pointer");
   JB_REQUIRE(!d || xo, "jb_add_rms: xo is needed with d");
   JB_REQUIRE(rows > 0 && n > 0 && n % 8 == 0 && n <= 128 * ew::RMS_MAX_VEC * 8, "jb_add_rms: rows %d, n %d", rows, n);
+  if (n == 1024) {
+    ew::add_rms_1024_kernel<<<(rows + 3) / 4, 128, 0, (cudaStream_t)stream>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(d), w1,
+        reinterpret_cast<__nv_bfloat16*>(xo), reinterpret_cast<__nv_bfloat16*>(h), rows);
+    return check_launch("add_rms_1024_kernel");
+  }
   ew::add_rms_kernel<<<rows, 128, 0, (cudaStream_t)stream>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(d), w1,
       reinterpret_cast<__nv_bfloat16*>(xo), reinterpret_cast<__nv_bfloat16*>(h), n);
