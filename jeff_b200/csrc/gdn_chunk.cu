@@ -102,6 +102,23 @@ __global__ void __launch_bounds__(256, 1) chunk_kernel(const __nv_bfloat16* __re
   const float scale = rsqrtf((float)D);
   const int stop = last ? min(last[row] + 1, n) : n;   // outputs past stop are written as zeros
 
+  // K, Q, V tiles of the chunk at c0 (zero past its end) into ks / qs / vs, asynchronously
+  auto issue_loads = [&](int c0) {
+    const int len = min(C, n - c0);
+    for (int i = threadIdx.x; i < 3 * C * (D / 8); i += 256) {
+      const int which = i / (C * (D / 8));
+      const int rem = i % (C * (D / 8));
+      const int t = rem / (D / 8), ch = rem % (D / 8);
+      const bool valid = t < len;
+      const size_t tok = (size_t)row * n + c0 + (valid ? t : 0);
+      const __nv_bfloat16* src = (which == 0 ? k : which == 1 ? q : v) + (tok * NH + h) * D + ch * 8;
+      __nv_bfloat16* dst = (which == 0 ? sm.ks : which == 1 ? sm.qs : sm.vs) + t * P16 + ch * 8;
+      cp_async16(dst, src, valid);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  issue_loads(0);   // in flight while the state loads
+
   // ---- the initial state: fp32 accumulators (warp w: key rows 16w + gr (+8), value cols 8nb + 2tq (+1))
   float s[16][4];
   {
@@ -129,17 +146,7 @@ __global__ void __launch_bounds__(256, 1) chunk_kernel(const __nv_bfloat16* __re
       *reinterpret_cast<uint32_t*>(&sm.sb[r0 * P16 + cc]) = pack_bf2(s[nb][0], s[nb][1]);
       *reinterpret_cast<uint32_t*>(&sm.sb[(r0 + 8) * P16 + cc]) = pack_bf2(s[nb][2], s[nb][3]);
     }
-    for (int i = threadIdx.x; i < 3 * C * (D / 8); i += 256) {
-      const int which = i / (C * (D / 8));
-      const int rem = i % (C * (D / 8));
-      const int t = rem / (D / 8), ch = rem % (D / 8);
-      const bool valid = t < len;
-      const size_t tok = (size_t)row * n + c0 + (valid ? t : 0);
-      const __nv_bfloat16* src = (which == 0 ? k : which == 1 ? q : v) + (tok * NH + h) * D + ch * 8;
-      __nv_bfloat16* dst = (which == 0 ? sm.ks : which == 1 ? sm.qs : sm.vs) + t * P16 + ch * 8;
-      cp_async16(dst, src, valid);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
+    // (this chunk's K, Q, V were issued before the state load or during the previous chunk's state update)
     if (threadIdx.x < C) {
       const int t = threadIdx.x;
       const size_t tok = (size_t)row * n + c0 + t;
@@ -200,19 +207,8 @@ __global__ void __launch_bounds__(256, 1) chunk_kernel(const __nv_bfloat16* __re
         }
     }
     __syncthreads();
-    // ---- scaled operand copies (the raw K and V are no longer needed after this)
-    for (int i = threadIdx.x; i < C * D / 2; i += 256) {
-      const int t = i / (D / 2), d = (i % (D / 2)) * 2;
-      const float eg = sm.eg[t], bt = sm.beta[t], ed = sm.ed[t];
-      const float k0 = __bfloat162float(sm.ks[t * P16 + d]), k1 = __bfloat162float(sm.ks[t * P16 + d + 1]);
-      const float q0 = __bfloat162float(sm.qs[t * P16 + d]), q1 = __bfloat162float(sm.qs[t * P16 + d + 1]);
-      const float v0 = __bfloat162float(sm.vs[t * P16 + d]), v1 = __bfloat162float(sm.vs[t * P16 + d + 1]);
-      *reinterpret_cast<uint32_t*>(&sm.kb[t * P16 + d]) = pack_bf2(k0 * bt * eg, k1 * bt * eg);
-      *reinterpret_cast<uint32_t*>(&sm.kd[t * P16 + d]) = pack_bf2(k0 * ed, k1 * ed);
-      *reinterpret_cast<uint32_t*>(&sm.qs[t * P16 + d]) = pack_bf2(q0 * eg, q1 * eg);
-      *reinterpret_cast<uint32_t*>(&sm.vs[t * P16 + d]) = pack_bf2(v0 * bt, v1 * bt);
-    }
-    // ---- T = (I - A)^-1: diagonal 16 x 16 blocks by column substitution (thread = block b, column j)
+    // ---- T = (I - A)^-1 diagonal 16 x 16 blocks (warps 0-1: thread = block b, column j, column substitution), while
+    // warps 2-7 make the scaled operand copies (the raw K and V are no longer needed after this)
     if (threadIdx.x < 64) {
       const int b = threadIdx.x >> 4, j = threadIdx.x & 15;
       const int base = 16 * b;
@@ -231,6 +227,18 @@ __global__ void __launch_bounds__(256, 1) chunk_kernel(const __nv_bfloat16* __re
       }
 #pragma unroll
       for (int i = 0; i < 16; ++i) sm.tf[(base + i) * PF + base + j] = col[i];
+    } else {
+      for (int i = threadIdx.x - 64; i < C * D / 2; i += 192) {
+        const int t = i / (D / 2), d = (i % (D / 2)) * 2;
+        const float eg = sm.eg[t], bt = sm.beta[t], ed = sm.ed[t];
+        const float k0 = __bfloat162float(sm.ks[t * P16 + d]), k1 = __bfloat162float(sm.ks[t * P16 + d + 1]);
+        const float q0 = __bfloat162float(sm.qs[t * P16 + d]), q1 = __bfloat162float(sm.qs[t * P16 + d + 1]);
+        const float v0 = __bfloat162float(sm.vs[t * P16 + d]), v1 = __bfloat162float(sm.vs[t * P16 + d + 1]);
+        *reinterpret_cast<uint32_t*>(&sm.kb[t * P16 + d]) = pack_bf2(k0 * bt * eg, k1 * bt * eg);
+        *reinterpret_cast<uint32_t*>(&sm.kd[t * P16 + d]) = pack_bf2(k0 * ed, k1 * ed);
+        *reinterpret_cast<uint32_t*>(&sm.qs[t * P16 + d]) = pack_bf2(q0 * eg, q1 * eg);
+        *reinterpret_cast<uint32_t*>(&sm.vs[t * P16 + d]) = pack_bf2(v0 * bt, v1 * bt);
+      }
     }
     __syncthreads();
     // off-diagonal blocks T_rc = T_rr (sum_{m=c}^{r-1} A_rm T_mc), by distance d = r - c from the diagonal: the
@@ -381,6 +389,8 @@ __global__ void __launch_bounds__(256, 1) chunk_kernel(const __nv_bfloat16* __re
         }
       }
     }
+    __syncthreads();   // every read of ks / qs / vs / ps of this chunk is done
+    if (c0 + C < n) issue_loads(c0 + C);   // the next chunk's tiles load during the state update
     // ---- S <- e^{gc_last} S + (e^{gc_last - gc} K)^T V'   (warp w: key rows 16w)
     const float el = expf(glast);
 #pragma unroll

@@ -211,15 +211,31 @@ def test_cfg4_chained_pass_matches_the_oracle_on_every_call(cfg4) -> None:
                                 adapters[rows.adapters[i] - 1].readout, adapters[rows.adapters[i] - 1].temperature,
                                 rows.counts[i], prefix_of[rows.adapters[i]]) for i in range(64)]
     ref = model_ref.run_pass(model, ref_rows)
-    diffs, agree = [], 0
+    diffs, agree, outcome_same, clear, clear_same, abstained, gaps = [], 0, 0, 0, 0, 0, []
     for i in range(64):
         c = rows.counts[i]
         g, w = torch.tensor(probs[i][:c].tolist()), ref.probs[i][:c]
         diffs.append(float((g - w).abs().max()))
         agree += int(torch.argmax(g) == torch.argmax(w))
-    print(f"chained pass: max |dp| {max(diffs):.4f}, mean {sum(diffs) / 64:.4f}, argmax agreement {agree}/64")
+        # the Decision outcome (decision.py:87-113): the chosen option, or an abstention below the threshold
+        gd, wd = model_ref.decision(g, c, THRESHOLD), model_ref.decision(w, c, THRESHOLD)
+        same = (gd[2] and wd[2]) or (not gd[2] and not wd[2] and gd[0] == wd[0])
+        outcome_same += int(same)
+        abstained += int(wd[2])
+        if torch.argmax(g) != torch.argmax(w):
+            srt = torch.sort(w.double() / w.double().sum(), descending=True).values
+            gaps.append(round(float(srt[0] - srt[1]), 4))
+        top = torch.topk(w.double() / w.double().sum(), min(2, c)).values
+        near = abs(wd[1] - THRESHOLD) < CHAIN_TOL or (not wd[2] and c > 1 and float(top[0] - top[1]) < CHAIN_TOL)
+        if not near:
+            clear += 1
+            clear_same += int(same)
+    print(f"chained pass: max |dp| {max(diffs):.4f}, mean {sum(diffs) / 64:.4f}, argmax agreement {agree}/64, "
+          f"decision/abstain outcome identical on {outcome_same}/64 ({clear_same}/{clear} away from the threshold "
+          f"and from ties; the oracle abstains on {abstained}); top-2 gaps where the argmax differs: {gaps}")
     assert max(diffs) < 5e-2
     assert agree >= 56, f"argmax agrees on {agree} of 64 calls"
+    assert clear_same == clear, f"decision outcome differs on {clear - clear_same} calls away from threshold and ties"
 
 
 def test_cfg4_graph_replays_are_deterministic_and_well_formed(cfg4) -> None:
