@@ -86,7 +86,8 @@ def call(name: str, *args) -> None:
     global launches
     lib = load()
     if name not in _NO_LAUNCH:
-        launches += 2 if (name == "jb_int4_lora_product" and args[11]) else 1   # args[11]: rank
+        products = ("jb_int4_lora_product", "jb_int4_lora_product_static")
+        launches += 2 if (name in products and args[11]) else 1   # args[11]: rank
     status = getattr(lib, name)(*args)
     if status != 0:
         msg = lib.jb_last_error().decode(errors="replace")
