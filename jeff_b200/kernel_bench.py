@@ -1,0 +1,134 @@
+"""Kernel throughput of the hot path's roofline targets on synthetic inputs shaped like the benchmark's
+configurations 1 and 3 (bench.py reports the whole decision pass; this reports single kernels against HBM).
+
+    python -m jeff_b200.kernel_bench [--reps N]
+
+cfg1: one int4 W4A16 + LoRA product: M 64 tokens, K 1024, N 3584, one rank-16 adapter, int4 group 128 with bf16
+  scales and zeros. Algorithmic bytes per call 2,686,976 (words 1,835,008 + scales 57,344 + zeros 57,344 + x 131,072
+  + y 458,752 + A 32,768 + B 114,688): HBM-bound. Timed as a CUDA graph of 256 calls cycling through enough distinct
+  weight copies to exceed twice the 126 MB L2, so each call streams its weights from HBM.
+cfg3: one Gated DeltaNet prefill layer: 64 rows x 256 new tokens, each from a pooled fp32 state ~ N(0, 0.1). The
+  prep kernel (conv width 4 + SiLU + L2 norms + gates from the projection output) reads 201 MB of q/k/v inputs,
+  1 MB of gates and 2.4 MB of convolution tails and writes 201 MB of q/k/v and 1.5 MB of g/beta; the chunked scan
+  reads q, k, v (201 MB), g and beta (1.5 MB) and the states (67 MB) and writes o (67 MB): 337 MB.
+
+One JSON line per kernel: milliseconds per call, GB/s of algorithmic bytes, and the fraction of the measured HBM copy
+bandwidth (MEASURED_PEAKS.json beside the repository root when present)."""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+from pathlib import Path
+
+import torch
+
+from jeff_b200 import constants as C
+from jeff_b200 import int4, kernels, synthetic
+from jeff_b200.prefix_pool import PrefixPool
+
+ROOT = Path(__file__).resolve().parent.parent
+L2_BYTES = 126 * 2**20
+
+
+def hbm_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def timed(fn, reps: int) -> float:
+    """Milliseconds per call of fn on the current stream (CUDA events, after 3 warm-up calls)."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        fn()
+    end.record()
+    end.synchronize()
+    return start.elapsed_time(end) / reps
+
+
+def cfg1(reps: int) -> dict:
+    m, k, n, rank = 64, 1024, 3584, 16
+    w = synthetic.normal(1, "cfg1/w", (n, k), 0.02)
+    packed, _ = int4.quantize_pack(w, "g128z")
+    per_copy = packed.words.numel() * 4 + packed.scales.numel() * 2 + packed.zeros.numel() * 2
+    copies = math.ceil(2 * L2_BYTES / per_copy)
+    dev = packed.to("cuda")
+    words = [kernels.int4_repack(dev.words.clone()) for _ in range(copies)]
+    scales = [dev.scales.clone() for _ in range(copies)]
+    zeros = [dev.zeros.clone() for _ in range(copies)]
+    a_pool = torch.zeros(2, rank, k, dtype=torch.bfloat16, device="cuda")
+    b_pool = torch.zeros(2, packed.columns, rank, dtype=torch.bfloat16, device="cuda")
+    a_pool[1] = synthetic.normal(1, "cfg1/a", (rank, k), 0.02).to(torch.bfloat16)
+    b_pool[1, :n] = (2.0 * synthetic.normal(1, "cfg1/b", (n, rank), 0.01)).to(torch.bfloat16)
+    adapters = torch.ones(1, dtype=torch.int32, device="cuda")
+    x = synthetic.normal(1, "cfg1/x", (m, k), 1.0).to(torch.bfloat16).cuda()
+    y = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+    mid = torch.empty(m, rank, dtype=torch.bfloat16, device="cuda")
+    calls = 256
+
+    def body() -> None:
+        for i in range(calls):
+            j = i % copies
+            kernels.int4_product(x, words[j], scales[j], zeros[j], packed.group, n, a_pool, b_pool, adapters, m,
+                                 mid=mid, y=y)
+
+    body()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        body()
+    ms = timed(graph.replay, reps) / calls
+    algo = 1_835_008 + 57_344 + 57_344 + 131_072 + 458_752 + 32_768 + 114_688
+    return {"kernel": "w4a16_lora (lora_shrink + w4a16_lora_kernel)", "config": "cfg1 M64 K1024 N3584 rank16 g128z",
+            "ms": ms, "bytes": algo, "weight_copies": copies}
+
+
+def cfg3(reps: int) -> list[dict]:
+    rows, n = 64, 256
+    t = rows * n
+    pool = PrefixPool(2 + rows * 51, "cuda")
+    slots = [pool.reserve(1, f"cfg3 state {i}", 1) for i in range(rows)]
+    g = torch.Generator(device="cuda").manual_seed(3)
+    pool.state.normal_(0.0, 0.1, generator=g)
+    pool.conv.normal_(0.0, 1.0, generator=g)
+    tables = pool.tables.index_select(0, torch.tensor(slots, device="cuda")).contiguous()
+    pr = torch.randn(t, C.GDN_PROJ, generator=g, device="cuda").to(torch.bfloat16)
+    conv_w = (0.5 * torch.randn(4, C.QKV_DIM, generator=g, device="cuda")).to(torch.bfloat16).float().contiguous()
+    a_neg = -torch.rand(C.NV, generator=g, device="cuda") * 16.0
+    dt_bias = torch.ones(C.NV, device="cuda")
+    outs = kernels.gdn_prep_rows(pr, pool, tables, 0, conv_w, a_neg, dt_bias, n)
+    o = torch.empty_like(outs[2])
+    prep_ms = timed(lambda: kernels.gdn_prep_rows(pr, pool, tables, 0, conv_w, a_neg, dt_bias, n, outs=outs), reps)
+    q, k, v, gg, beta = outs
+    scan_ms = timed(lambda: kernels.gdn_scan(q, k, v, gg, beta, pool, tables, 0, out=o), reps)
+    qkv = t * C.QKV_DIM * 2
+    prep_bytes = qkv + t * 2 * C.NV * 2 + rows * 3 * C.QKV_DIM * 2 + 4 * C.QKV_DIM * 4 + qkv + t * C.NV * (4 + 2)
+    scan_bytes = qkv + t * C.NV * (4 + 2) + rows * C.NV * C.DK * C.DV * 4 + t * C.NV * C.DV * 2
+    return [{"kernel": "gdn prep_kernel", "config": "cfg3 64 rows x 256 tokens", "ms": prep_ms, "bytes": prep_bytes},
+            {"kernel": "gdn chunk_kernel (scan from pooled state)", "config": "cfg3 64 rows x 256 tokens",
+             "ms": scan_ms, "bytes": scan_bytes}]
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reps", type=int, default=20)
+    args = ap.parse_args()
+    if not torch.cuda.is_available():
+        raise SystemExit("kernel_bench needs a CUDA GPU")
+    torch.cuda.set_device(0)
+    peak, source = hbm_peak()
+    for line in [cfg1(args.reps), *cfg3(args.reps)]:
+        gbs = line["bytes"] / (line["ms"] / 1e3) / 1e9
+        line.update(gbs=gbs, hbm_peak_gbs=peak, peak_source=source, frac=gbs / peak)
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()
