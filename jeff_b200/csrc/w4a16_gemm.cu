@@ -491,11 +491,14 @@ __global__ void __launch_bounds__(128) lora_shrink_kernel(const __nv_bfloat16* _
 
 // ------------------------------------------------------------------ LoRA shrink, staged
 //
-// The same product for blocks of 64 rows that share one adapter (row_len a multiple of 64, K a multiple of 128):
-// 8 warps, warp w on rows 16 (w & 3) .. + 16 and on the K half w >> 2 of every 128-wide K step; the block's x rows and
+// The same product for blocks of 32 rows that share one adapter (row_len a multiple of 32, K a multiple of 128):
+// 4 warps, warp w on rows 16 (w & 1) .. + 16 and on the K half w >> 1 of every 128-wide K step; the block's x rows and
 // its adapter's A rows for each K step are staged in shared memory by cp.async (double-buffered) and read by
-// ldmatrix. The two K halves' float32 partials are added in a fixed order: deterministic.
-constexpr int SH_ROWS = 64, SH_BK = 128, SH_PITCH = SH_BK + 8;   // 272-B rows: ldmatrix without bank conflicts
+// ldmatrix. The two K halves' float32 partials are added in a fixed order: deterministic. Small blocks keep several
+// CTAs resident per SM, so the loads of many blocks overlap.
+constexpr int SH_ROWS = 32, SH_BK = 128, SH_PITCH = SH_BK + 8;   // 272-B rows: ldmatrix without bank conflicts
+constexpr int SH_THREADS = 128;   // 4 warps: 2 groups of 16 rows x 2 halves of each 128-wide K step
+constexpr int SH_STAGES = 4;      // cp.async ring: three K steps in flight while one is multiplied
 
 __device__ __forceinline__ void sh_cp16(void* dst, const void* src, bool valid) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(valid ? 16 : 0)
@@ -516,21 +519,21 @@ __device__ __forceinline__ void sh_mma(float (&c)[4], const uint32_t (&a)[4], ui
 
 template <int NB>
 constexpr int shrink_staged_smem() {
-  return (2 * SH_ROWS * SH_PITCH + 2 * NB * 8 * SH_PITCH) * 2;
+  return (SH_STAGES * SH_ROWS * SH_PITCH + SH_STAGES * NB * 8 * SH_PITCH) * 2;
 }
 
 template <int NB>
-__global__ void __launch_bounds__(256) lora_shrink_staged_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
+__global__ void __launch_bounds__(SH_THREADS) lora_shrink_staged_kernel(const __nv_bfloat16* __restrict__ x, int M, int K,
                                                                  const __nv_bfloat16* __restrict__ A, int pool_rows,
                                                                  const int* __restrict__ adapters, int row_len,
                                                                  __nv_bfloat16* __restrict__ mid) {
   constexpr int R = NB * 8;
   extern __shared__ __align__(16) uint8_t sh_smem[];
-  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sh_smem);   // [2][64][SH_PITCH]
-  __nv_bfloat16* as = xs + 2 * SH_ROWS * SH_PITCH;                 // [2][R][SH_PITCH]
-  float* red = reinterpret_cast<float*>(sh_smem);                  // after the K loop: [64][R + 4]
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sh_smem);   // [SH_STAGES][SH_ROWS][SH_PITCH]
+  __nv_bfloat16* as = xs + SH_STAGES * SH_ROWS * SH_PITCH;         // [SH_STAGES][R][SH_PITCH]
+  float* red = reinterpret_cast<float*>(sh_smem);                  // after the K loop: [SH_ROWS][R + 4]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rg = warp & 3, kh = warp >> 2;
+  const int rg = warp & 1, kh = warp >> 1;
   const int m0 = blockIdx.x * SH_ROWS;
   int a = adapters[m0 / row_len];
   if (a < 0 || a >= pool_rows) a = 0;
@@ -541,12 +544,12 @@ __global__ void __launch_bounds__(256) lora_shrink_staged_kernel(const __nv_bflo
     const int k0 = kb * SH_BK;
     __nv_bfloat16* xd = xs + buf * SH_ROWS * SH_PITCH;
     __nv_bfloat16* ad = as + buf * R * SH_PITCH;
-    for (int i = threadIdx.x; i < SH_ROWS * 16; i += 256) {
+    for (int i = threadIdx.x; i < SH_ROWS * 16; i += SH_THREADS) {
       const int r = i >> 4, c = i & 15;
       const bool valid = m0 + r < M;
       sh_cp16(xd + r * SH_PITCH + c * 8, x + (size_t)(valid ? m0 + r : 0) * K + k0 + c * 8, valid);
     }
-    for (int i = threadIdx.x; i < R * 16; i += 256) {
+    for (int i = threadIdx.x; i < R * 16; i += SH_THREADS) {
       const int r = i >> 4, c = i & 15;
       sh_cp16(ad + r * SH_PITCH + c * 8, Aa + (size_t)r * K + k0 + c * 8, true);
     }
@@ -556,17 +559,18 @@ __global__ void __launch_bounds__(256) lora_shrink_staged_kernel(const __nv_bflo
   float acc[NB][4];
 #pragma unroll
   for (int i = 0; i < NB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-  stage(0, 0);
+  // prologue: K steps 0 .. SH_STAGES - 2 in flight (an empty group where K runs out keeps the group count)
+  for (int st = 0; st < SH_STAGES - 1; ++st) {
+    if (st < nk) stage(st, st);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+  }
   for (int kb = 0; kb < nk; ++kb) {
-    if (kb + 1 < nk) {
-      stage(kb + 1, (kb + 1) & 1);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
-    __syncthreads();
-    const __nv_bfloat16* xb = xs + (kb & 1) * SH_ROWS * SH_PITCH;
-    const __nv_bfloat16* ab = as + (kb & 1) * R * SH_PITCH;
+    asm volatile("cp.async.wait_group %0;" ::"n"(SH_STAGES - 2) : "memory");   // step kb has landed
+    __syncthreads();   // ... for every thread; and every warp is done with step kb - 1, whose buffer refills now
+    if (kb + SH_STAGES - 1 < nk) stage(kb + SH_STAGES - 1, (kb + SH_STAGES - 1) % SH_STAGES);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    const __nv_bfloat16* xb = xs + (kb % SH_STAGES) * SH_ROWS * SH_PITCH;
+    const __nv_bfloat16* ab = as + (kb % SH_STAGES) * R * SH_PITCH;
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
       const int kc = kh * 64 + kk * 16;
@@ -581,8 +585,9 @@ __global__ void __launch_bounds__(256) lora_shrink_staged_kernel(const __nv_bflo
         sh_mma(acc[nb + 1], af, bfr[2], bfr[3]);
       }
     }
-    __syncthreads();   // every warp is done with this buffer before the next stage() refills it
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  __syncthreads();   // every warp is done with the staging buffers before the partials reuse them
   const int g = lane >> 2, t = lane & 3;
   constexpr int RP = R + 4;
   if (kh == 1) {
@@ -622,7 +627,7 @@ int launch_shrink_staged(const __nv_bfloat16* x, int m, int k, const __nv_bfloat
   cudaError_t e = cudaFuncSetAttribute(lora_shrink_staged_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        bytes);
   if (e != cudaSuccess) return status_of(e, "lora_shrink_staged_kernel: shared memory attribute");
-  lora_shrink_staged_kernel<NB><<<(m + SH_ROWS - 1) / SH_ROWS, 256, bytes, st>>>(x, m, k, a, pool_rows, adapters,
+  lora_shrink_staged_kernel<NB><<<(m + SH_ROWS - 1) / SH_ROWS, SH_THREADS, bytes, st>>>(x, m, k, a, pool_rows, adapters,
                                                                                  row_len, mid);
   return check_launch("lora_shrink_staged_kernel");
 }

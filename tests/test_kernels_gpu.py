@@ -192,11 +192,12 @@ def test_int4_lora_product_swiglu_epilogue(fmt: str) -> None:
 
 
 @pytest.mark.parametrize(("m", "k", "rank", "row_len"), [
-    (256, 1024, 48, 64),      # staged kernel (64-row blocks of one adapter)
+    (256, 1024, 48, 64),      # staged kernel (32-row blocks of one adapter)
     (512, 3584, 16, 128),     # staged, K = 3584
-    (208, 2048, 64, 64),      # staged, m not a multiple of the 64-row block
+    (208, 2048, 64, 64),      # staged, m not a multiple of the 32-row block
     (384, 1024, 32, 128),     # staged
-    (256, 1024, 48, 32),      # 16-row kernel: rows of 32 tokens
+    (256, 1024, 48, 32),      # staged, rows of 32 tokens
+    (96, 1024, 32, 16),       # 16-row kernel: rows of 16 tokens
     (96, 960, 16, 32),        # 16-row kernel: K not a multiple of 128
 ])
 def test_lora_shrink_matches_the_oracle(m: int, k: int, rank: int, row_len: int) -> None:
