@@ -18,7 +18,7 @@ namespace gdnc {
 constexpr int C = 64, D = 128, NH = 16;
 constexpr int P16 = D + 8;              // bf16 row pitch (elements) of 128-wide tiles: 272 B, ldmatrix conflict-free
 constexpr int P64 = C + 8;              // bf16 row pitch of 64-wide tiles: 144 B
-constexpr int PF = C + 1;               // fp32 row pitch of 64-wide tiles
+constexpr int PF = C + 4;               // fp32 row pitch of 64-wide tiles (rows 16-byte aligned)
 constexpr size_t STATE_BYTES = (size_t)D * D * 4;
 
 struct Smem {
@@ -242,28 +242,42 @@ __global__ void __launch_bounds__(256, 1) chunk_kernel(const __nv_bfloat16* __re
     }
     __syncthreads();
     // off-diagonal blocks T_rc = T_rr (sum_{m=c}^{r-1} A_rm T_mc), by distance d = r - c from the diagonal: the
-    // blocks of one distance need only blocks nearer the diagonal, so each distance is one parallel step
+    // blocks of one distance need only blocks nearer the diagonal, so each distance is one parallel step. Thread =
+    // (block c of the step, row i, 4 adjacent columns 4 q .. 4 q + 3): one load of A and one 16-byte load of T feed
+    // four independent sums, each summed in the same order as an element-by-element loop.
     {
-      const int i = threadIdx.x >> 4, j = threadIdx.x & 15;   // element of a 16 x 16 block
+      const int bc = threadIdx.x >> 6, i = (threadIdx.x >> 2) & 15, q4 = (threadIdx.x & 3) * 4;
       for (int d = 1; d < 4; ++d) {
-        for (int c = 0; c + d < 4; ++c) {
-          const int r = c + d;
-          float tmp = 0.f;
+        const int c = bc, r = c + d;
+        const bool active = c + d < 4;
+        if (active) {
+          float4 tmp = make_float4(0.f, 0.f, 0.f, 0.f);
           for (int m = c; m < r; ++m)
 #pragma unroll
-            for (int kx = 0; kx < 16; ++kx)
-              tmp += sm.amat[(16 * r + i) * PF + 16 * m + kx] * sm.tf[(16 * m + kx) * PF + 16 * c + j];
+            for (int kx = 0; kx < 16; ++kx) {
+              const float av = sm.amat[(16 * r + i) * PF + 16 * m + kx];
+              const float4 tv = *reinterpret_cast<const float4*>(&sm.tf[(16 * m + kx) * PF + 16 * c + q4]);
+              tmp.x += av * tv.x;
+              tmp.y += av * tv.y;
+              tmp.z += av * tv.z;
+              tmp.w += av * tv.w;
+            }
           // staged in block (c, r) of amat's strictly upper part, which holds nothing
-          sm.amat[(16 * c + i) * PF + 16 * r + j] = tmp;
+          *reinterpret_cast<float4*>(&sm.amat[(16 * c + i) * PF + 16 * r + q4]) = tmp;
         }
         __syncthreads();
-        for (int c = 0; c + d < 4; ++c) {
-          const int r = c + d;
-          float acc = 0.f;
+        if (active) {
+          float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-          for (int kx = 0; kx < 16; ++kx)
-            acc += sm.tf[(16 * r + i) * PF + 16 * r + kx] * sm.amat[(16 * c + kx) * PF + 16 * r + j];
-          sm.tf[(16 * r + i) * PF + 16 * c + j] = acc;
+          for (int kx = 0; kx < 16; ++kx) {
+            const float tv = sm.tf[(16 * r + i) * PF + 16 * r + kx];
+            const float4 av = *reinterpret_cast<const float4*>(&sm.amat[(16 * c + kx) * PF + 16 * r + q4]);
+            acc.x += tv * av.x;
+            acc.y += tv * av.y;
+            acc.z += tv * av.z;
+            acc.w += tv * av.w;
+          }
+          *reinterpret_cast<float4*>(&sm.tf[(16 * r + i) * PF + 16 * c + q4]) = acc;
         }
         __syncthreads();
       }
