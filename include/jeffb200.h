@@ -51,8 +51,11 @@ int jb_int4_dequant(const int32_t* words, const uint16_t* scales, const uint16_t
                     int group, uint16_t* out, void* stream);
 
 /* LoRA first factor: mid (m, rank) bf16 = bf16(x (m, k) . A[a]^T) with fp32 accumulation in input order, A from
- * lora_a (pool_rows, rank, k) in the row a = adapters[t / row_len] of token t. Replaces fast_path._lora_mid_kernel
- * (fast_path.py:159-177) and int4_kernels._lora_mid_tile (int4_kernels.py:65-82). */
+ * lora_a (pool_rows, rank, k) in the row a = adapters[t / row_len] of token t (an id outside [0, pool_rows) reads
+ * row 0). Any row_len >= 1 when k % 128 == 0, row_len = 1 being one adapter id per token (requests of mixed lengths
+ * packed back to back); a row's bits do not depend on row_len or on its neighbours. Otherwise m and row_len must be
+ * multiples of 16. Replaces fast_path._lora_mid_kernel (fast_path.py:159-177) and int4_kernels._lora_mid_tile
+ * (int4_kernels.py:65-82), whose tiles need row_len to be a multiple of their height (fast_path.py:225-227). */
 int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* lora_a, int rank, int pool_rows,
                    const int32_t* adapters, int row_len, uint16_t* mid, void* stream);
 
@@ -60,9 +63,11 @@ int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* lora_a, int 
  * scales, zeros as jb_int4_dequant), the base product accumulated in fp32 by tcgen05 tensor cores from TMA-staged
  * packed weights dequantised in shared memory, then the LoRA expand (mid from jb_lora_shrink, B from lora_b (pool_rows, columns,
  * rank)) added into the same accumulator, rounded once. rank 0 (or mid NULL) leaves out the LoRA term.
- * Requires k % 64 == 0, columns % 64 == 0, out <= columns, ldy % 8 == 0, row_len % 32 == 0 and row_len % 128 == 0
- * or 128 % row_len == 0. Replaces int4_kernels.int4_product (int4_kernels.py:132-177) and Lin.__call__
- * (fast_path.py:347-349). */
+ * Requires k % 64 == 0, columns % 64 == 0, out <= columns, ldy % 8 == 0 and row_len >= 1. With row_len % 128 == 0
+ * the expand operands are loaded by TMA (one adapter per 128-row half); with any other row_len (down to 1: one
+ * adapter id per token) they are gathered per 256-row tile from that tile's adapters, which needs pool_rows <= 256
+ * and m <= 32768. Both give a row the same bits. Replaces int4_kernels.int4_product (int4_kernels.py:132-177) and
+ * Lin.__call__ (fast_path.py:347-349). */
 int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
                   const uint16_t* zeros, int group, int columns, int out, const uint16_t* mid, const uint16_t* lora_b,
                   int rank, int pool_rows, const int32_t* adapters, int row_len, uint16_t* y, int ldy, int flags,

@@ -12,11 +12,16 @@
 //                tile's main loop); one thread issues tcgen05.mma (M=128, N=128, K=16) x 4 x 2 per K block;
 //   warps 2-9    two groups of four, each on alternate K blocks (two stages dequantised at once): each stage's
 //                words into bf16 in the UMMA 128B-swizzled K-major layout (deq[s]).
-// The LoRA expand runs as extra K blocks of the same accumulator: the x slot holds each row's mid in its
-// adapter's rank block and the weight slot those adapters' B rows (columns [half 0 adapters | half 1 adapters],
-// zeros elsewhere: exact). With one adapter per 128-row half (rows of >= 128 tokens) the producer instead loads each
-// half's mid rows and its adapter's B rows by TMA as planes of 8 columns, and each half's expand is an MMA of its own
-// (no zero blocks); otherwise the dequantisers gather the block-diagonal operands.
+// The LoRA expand runs as extra K blocks of the same accumulator. With one adapter per 128-row half (rows whose
+// length is a multiple of 128 tokens) the producer loads each half's mid rows and its adapter's B rows by TMA as
+// planes of 8 columns, and each half's expand is an MMA of its own. Otherwise (any other row length, down to one
+// adapter id per token for packed requests of mixed lengths) the dequantisers gather the operands: the tile's
+// distinct adapters, in pool-row order, each own `rank` expand columns; the x slot holds each row's mid in its
+// adapter's block (zeros elsewhere: exact) and the weight slot those adapters' B rows. The tile's adapter set comes
+// from a bitmask over pool rows per 256-row tile, built once at kernel start, so every role derives the
+// same number of expand blocks for a tile. Every block starts at a multiple of 16 expand columns, so a row's own
+// terms meet the tensor core in the same K16 positions whichever adapters share its tile: its bits do not depend
+// on the other rows of the pass.
 //   warps 10-13  epilogue: TMEM -> registers -> bf16 -> 16-byte stores of each row (clipped to M x out), then the
 //                accumulator is released (tmem_empty). With `swiglu` the 128 columns are 64 gate | 64 up columns of
 //                the interleaved gate/up group and the tile's 64 outputs are bf16(bf16(silu(g)) u) (the reference's
@@ -40,7 +45,8 @@ constexpr int GROUPS = 2;          // dequantiser groups, each on alternate K bl
 constexpr int DEQ_WARPS = 8;
 constexpr int EPI_WARPS = 4;
 constexpr int THREADS = 64 + (DEQ_WARPS + EPI_WARPS) * 32;
-constexpr int MAX_EXPAND = 192;     // adapters per half x rank (the expand uses twice that: both halves' adapters)
+constexpr int MASK_WORDS = 8;       // gathered expand: a tile's adapter set as a bitmask over pool rows < 256
+constexpr int MAX_MASK_TILES = 128; // ... for up to 128 row tiles (m <= 32768)
 
 struct Params {
   int M, K, columns, out, group;
@@ -71,7 +77,8 @@ struct Layout {
   static constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
   static constexpr int OFF_ADP = OFF_MISC + 16;
   static constexpr int MAX_ROWS = 512;            // adapter indices staged in shared memory (M / row_len rows)
-  static constexpr int BYTES = OFF_ADP + MAX_ROWS * 4;
+  static constexpr int OFF_MASK = OFF_ADP + MAX_ROWS * 4;
+  static constexpr int BYTES = OFF_MASK + MAX_MASK_TILES * MASK_WORDS * 4;
   static constexpr int ALLOC = BYTES + 1024;       // room to align the base to 1024 B
   static_assert(ALLOC <= 227 * 1024, "shared memory");
 };
@@ -95,6 +102,32 @@ __device__ __forceinline__ uint4 dequant8(uint32_t w, __nv_bfloat162 s2, __nv_bf
 __device__ __forceinline__ __nv_bfloat162 zero_pair(const __nv_bfloat16* zr, int n) {
   float z = zr ? __bfloat162float(zr[n]) : 8.0f;
   return __floats2bfloat162_rn(128.0f + z, 128.0f + z);
+}
+
+// a row tile's adapter set (MASK_WORDS words, bit a for pool row a): its size, the number of members below a, and
+// its j-th member in increasing order (j < the size)
+__device__ __forceinline__ int mask_count(const uint32_t* mask) {
+  int d = 0;
+#pragma unroll
+  for (int w = 0; w < MASK_WORDS; ++w) d += __popc(mask[w]);
+  return d;
+}
+__device__ __forceinline__ int mask_rank(const uint32_t* mask, int a) {
+  int r = __popc(mask[a >> 5] & ((1u << (a & 31)) - 1u));
+  for (int w = 0; w < (a >> 5); ++w) r += __popc(mask[w]);
+  return r;
+}
+__device__ __forceinline__ int mask_nth(const uint32_t* mask, int j) {
+  for (int w = 0; w < MASK_WORDS; ++w) {
+    uint32_t m = mask[w];
+    const int c = __popc(m);
+    if (j < c) {
+      for (int i = 0; i < j; ++i) m &= m - 1u;   // drop the j lowest members
+      return 32 * w + __ffs(m) - 1;
+    }
+    j -= c;
+  }
+  return 0;
 }
 
 __device__ __forceinline__ float silu_rounded(float g) { return round_bf(g / (1.0f + expf(-g))); }
@@ -122,25 +155,50 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int nkb = p.K / BK;
   const bool has_lora = p.mid != nullptr && p.rank > 0;
-  const int n_adp = p.row_len >= HM ? 1 : HM / p.row_len;   // adapters per 128-row half
-  const int ke_half = has_lora ? n_adp * p.rank : 0;         // expand columns per half
-  const int ke = 2 * ke_half;                                 // both halves' adapters
-  // one adapter per 128-row half (row_len >= 128): the producer loads each half's mid rows and its adapter's B
-  // rows by TMA, and each half's expand is its own MMA of depth rank (both halves in one K block when 2 rank <= 64,
-  // else one block each); otherwise the dequantisers gather block-diagonal operands (see below)
-  const bool lora_tma = has_lora && p.row_len >= HM;
+  // rows whose length is a multiple of 128 tokens (one adapter per 128-row half): the producer loads each half's
+  // mid rows and its adapter's B rows by TMA, and each half's expand is its own MMA of depth rank (both halves in
+  // one K block when 2 rank <= 64, else one block each); otherwise the dequantisers gather the operands (below)
+  const bool lora_tma = has_lora && p.row_len % HM == 0;
+  const bool gathered = has_lora && !lora_tma;
   const bool halves_together = 2 * p.rank <= BK;
-  const int nlb = lora_tma ? (halves_together ? 1 : 2) : (ke + BK - 1) / BK;   // LoRA K blocks
-  const int nkt = nkb + nlb;                                  // K blocks per tile
   const int tiles = p.m_tiles * p.n_tiles;
   int* s_adp = reinterpret_cast<int*>(smem + L::OFF_ADP);
-  if (has_lora) {
+  uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem + L::OFF_MASK);   // [m tile][MASK_WORDS]
+  if (lora_tma) {
     const int rows = (p.M + p.row_len - 1) / p.row_len;
     for (int i = threadIdx.x; i < rows && i < L::MAX_ROWS; i += blockDim.x) {
       const int a = p.adapters[i];
       s_adp[i] = (a >= 0 && a < p.pool_rows) ? a : -1;
     }
   }
+  if (gathered) {
+    // each row tile's adapter set: bit a of the tile's mask for every valid adapter a of a token in the tile. A warp
+    // takes 32 consecutive request rows; of a run of lanes with the same (tile, adapter) only the first one sets the
+    // bit, so packed requests cost one shared atomic per run.
+    for (int i = threadIdx.x; i < p.m_tiles * MASK_WORDS; i += blockDim.x) s_mask[i] = 0;
+    __syncthreads();
+    const int rows = (p.M + p.row_len - 1) / p.row_len;
+    for (int r0 = warp * 32; r0 < rows; r0 += blockDim.x) {
+      const int r = r0 + lane;
+      int a = r < rows ? p.adapters[r] : -1;
+      if (a >= p.pool_rows) a = -1;
+      const int t0 = a >= 0 ? r * p.row_len : 0;                // the row's first token (< M) ...
+      const int t1 = a >= 0 ? t0 + min(p.row_len, p.M - t0) - 1 : 0;   // ... and its last
+      const int key = a >= 0 ? (t0 / BM) * 256 + a : -1;
+      const int prev = __shfl_up_sync(0xffffffffu, key, 1);
+      if (a >= 0) {
+        const uint32_t bit = 1u << (a & 31);
+        if (lane == 0 || prev != key) atomicOr(&s_mask[(t0 / BM) * MASK_WORDS + (a >> 5)], bit);
+        for (int mt = t0 / BM + 1; mt <= t1 / BM; ++mt) atomicOr(&s_mask[mt * MASK_WORDS + (a >> 5)], bit);
+      }
+    }
+  }
+  // the K blocks of a tile of row tile mt: the base product's, then the expand's
+  auto lora_blocks = [&](int mt) -> int {
+    if (lora_tma) return halves_together ? 1 : 2;
+    if (!gathered) return 0;
+    return (mask_count(s_mask + mt * MASK_WORDS) * p.rank + BK - 1) / BK;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -161,7 +219,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     prefetch_tmap(&tm_w);
     prefetch_tmap(&tm_s);
     if (ZERO) prefetch_tmap(&tm_z);
-    if (has_lora && p.row_len >= HM) {
+    if (lora_tma) {
       prefetch_tmap(&tm_mid);
       prefetch_tmap(&tm_lb);
     }
@@ -182,6 +240,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t kg = 0;
       for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
         const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
+        const int nkt = nkb + lora_blocks(tile % p.m_tiles);
         for (int kb = 0; kb < nkt; ++kb, ++kg) {
           const int s = kg % STAGES;
           if (!mbar_wait(&empty[s], ((kg / STAGES) & 1) ^ 1, abort_flag, p.err, 1)) break;
@@ -233,6 +292,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (!ok) break;
         tc_fence_after();
         const uint32_t acc = tmem + b * 2 * BN;
+        const int nkt = nkb + lora_blocks(tile % p.m_tiles);
         for (int kb = 0; kb < nkt; ++kb, ++kg) {
           const int s = kg % STAGES;
           const uint32_t ph = (kg / STAGES) & 1;
@@ -273,7 +333,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint32_t kg = 0;
     bool ok = true;
     for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-      const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
+      const int mt = tile % p.m_tiles;
+      const int m0 = mt * BM, n0 = (tile / p.m_tiles) * BN;
+      const int nkt = nkb + lora_blocks(mt);
       for (int kb = 0; kb < nkt; ++kb, ++kg) {
         if ((int)(kg % GROUPS) != grp) continue;
         const int s = kg % STAGES;
@@ -294,8 +356,12 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int r = 0; r < 8; ++r)
             *reinterpret_cast<uint4*>(wt + sw128_offset(n, r)) = dequant8(w[r], s2, zb2);
         } else if (!lora_tma) {
-          // LoRA block: expand columns [col0, col0 + 64) of [half 0 adapters | half 1 adapters]. Every global load
-          // of the block is issued before any store, so their latencies overlap.
+          // LoRA block, gathered: expand columns [col0, col0 + 64) of the tile's adapters in pool-row order, rank
+          // columns each. Row lrow of each half puts its mid in its adapter's block; weight column n holds each
+          // block's adapter's B row. Every global load of the block is issued before any store, so their
+          // latencies overlap.
+          const uint32_t* mask = s_mask + mt * MASK_WORDS;
+          const int ke = mask_count(mask) * p.rank;    // expand columns of this tile
           const int col0 = (kb - nkb) * BK;
           const int lrow = n;
           const int gn = n0 + n;
@@ -303,13 +369,15 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             const int gm = m0 + h * HM + lrow;
-            const int block_of_row = h * n_adp + ((p.row_len >= HM) ? 0 : lrow / p.row_len);
+            int a = gm < p.M ? p.adapters[gm / p.row_len] : -1;
+            if (a >= p.pool_rows) a = -1;
+            const int lo = a >= 0 ? mask_rank(mask, a) * p.rank : 0;   // the row's block: [lo, lo + rank)
 #pragma unroll
             for (int c8 = 0; c8 < 8; ++c8) {
               const int col = col0 + 8 * c8;
               xv[h][c8] = make_uint4(0, 0, 0, 0);
-              if (col < ke && gm < p.M && col / p.rank == block_of_row)
-                xv[h][c8] = *reinterpret_cast<const uint4*>(p.mid + (size_t)gm * p.rank + (col % p.rank));
+              if (a >= 0 && col >= lo && col < lo + p.rank)
+                xv[h][c8] = *reinterpret_cast<const uint4*>(p.mid + (size_t)gm * p.rank + (col - lo));
             }
           }
 #pragma unroll
@@ -317,15 +385,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int col = col0 + 8 * c8;
             wv[c8] = make_uint4(0, 0, 0, 0);
             if (col < ke && gn < p.columns) {
-              const int blk = col / p.rank;
-              const int hh = blk / n_adp, j = blk % n_adp;
-              const int first_row = m0 + hh * HM + j * (p.row_len >= HM ? 0 : p.row_len);
-              if (first_row < p.M) {
-                const int a = s_adp[first_row / p.row_len];
-                if (a >= 0)
-                  wv[c8] = *reinterpret_cast<const uint4*>(p.lora_b + ((size_t)a * p.columns + gn) * p.rank +
-                                                           (col % p.rank));
-              }
+              const int a = mask_nth(mask, col / p.rank);
+              wv[c8] = *reinterpret_cast<const uint4*>(p.lora_b + ((size_t)a * p.columns + gn) * p.rank +
+                                                       (col % p.rank));
             }
           }
 #pragma unroll
@@ -491,11 +553,14 @@ __global__ void __launch_bounds__(128) lora_shrink_kernel(const __nv_bfloat16* _
 
 // ------------------------------------------------------------------ LoRA shrink, staged
 //
-// The same product for blocks of 32 rows that share one adapter (row_len a multiple of 32, K a multiple of 128):
-// 4 warps, warp w on rows 16 (w & 1) .. + 16 and on the K half w >> 1 of every 128-wide K step; the block's x rows and
-// its adapter's A rows for each K step are staged in shared memory by cp.async (double-buffered) and read by
-// ldmatrix. The two K halves' float32 partials are added in a fixed order: deterministic. Small blocks keep several
-// CTAs resident per SM, so the loads of many blocks overlap.
+// The same product in blocks of 32 rows (K a multiple of 128, any row length): 4 warps, warp w on rows 16 (w & 1)
+// .. + 16 and on the K half w >> 1 of every 128-wide K step; the block's x rows and its adapter's A rows for each K
+// step are staged in shared memory by cp.async (a four-deep ring) and read by ldmatrix. The two K halves' float32
+// partials are added in a fixed order: deterministic. A block whose rows belong to several adapters (short rows,
+// or one adapter id per token for packed requests of mixed lengths) runs the K loop once per distinct adapter and
+// keeps each row from its own adapter's pass; every row goes through the same instructions in the same order
+// either way, so its bits are those of a block of one adapter. Small blocks keep several CTAs resident per SM, so
+// the loads of many blocks overlap.
 constexpr int SH_ROWS = 32, SH_BK = 128, SH_PITCH = SH_BK + 8;   // 272-B rows: ldmatrix without bank conflicts
 constexpr int SH_THREADS = 128;   // 4 warps: 2 groups of 16 rows x 2 halves of each 128-wide K step
 constexpr int SH_STAGES = 4;      // cp.async ring: three K steps in flight while one is multiplied
@@ -532,89 +597,106 @@ __global__ void __launch_bounds__(SH_THREADS) lora_shrink_staged_kernel(const __
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sh_smem);   // [SH_STAGES][SH_ROWS][SH_PITCH]
   __nv_bfloat16* as = xs + SH_STAGES * SH_ROWS * SH_PITCH;         // [SH_STAGES][R][SH_PITCH]
   float* red = reinterpret_cast<float*>(sh_smem);                  // after the K loop: [SH_ROWS][R + 4]
+  __shared__ int row_adp[SH_ROWS], set[SH_ROWS], set_size;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rg = warp & 1, kh = warp >> 1;
   const int m0 = blockIdx.x * SH_ROWS;
-  int a = adapters[m0 / row_len];
-  if (a < 0 || a >= pool_rows) a = 0;
-  const __nv_bfloat16* Aa = A + (size_t)a * R * K;
   const int nk = K / SH_BK;
-
-  auto stage = [&](int kb, int buf) {
-    const int k0 = kb * SH_BK;
-    __nv_bfloat16* xd = xs + buf * SH_ROWS * SH_PITCH;
-    __nv_bfloat16* ad = as + buf * R * SH_PITCH;
-    for (int i = threadIdx.x; i < SH_ROWS * 16; i += SH_THREADS) {
-      const int r = i >> 4, c = i & 15;
-      const bool valid = m0 + r < M;
-      sh_cp16(xd + r * SH_PITCH + c * 8, x + (size_t)(valid ? m0 + r : 0) * K + k0 + c * 8, valid);
-    }
-    for (int i = threadIdx.x; i < R * 16; i += SH_THREADS) {
-      const int r = i >> 4, c = i & 15;
-      sh_cp16(ad + r * SH_PITCH + c * 8, Aa + (size_t)r * K + k0 + c * 8, true);
-    }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-
-  float acc[NB][4];
-#pragma unroll
-  for (int i = 0; i < NB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
-  // prologue: K steps 0 .. SH_STAGES - 2 in flight (an empty group where K runs out keeps the group count)
-  for (int st = 0; st < SH_STAGES - 1; ++st) {
-    if (st < nk) stage(st, st);
-    else asm volatile("cp.async.commit_group;" ::: "memory");
-  }
-  for (int kb = 0; kb < nk; ++kb) {
-    asm volatile("cp.async.wait_group %0;" ::"n"(SH_STAGES - 2) : "memory");   // step kb has landed
-    __syncthreads();   // ... for every thread; and every warp is done with step kb - 1, whose buffer refills now
-    if (kb + SH_STAGES - 1 < nk) stage(kb + SH_STAGES - 1, (kb + SH_STAGES - 1) % SH_STAGES);
-    else asm volatile("cp.async.commit_group;" ::: "memory");
-    const __nv_bfloat16* xb = xs + (kb % SH_STAGES) * SH_ROWS * SH_PITCH;
-    const __nv_bfloat16* ab = as + (kb % SH_STAGES) * R * SH_PITCH;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const int kc = kh * 64 + kk * 16;
-      uint32_t af[4];
-      sh_ldsm4(xb + (rg * 16 + (lane & 15)) * SH_PITCH + kc + (lane >> 4) * 8, af);
-#pragma unroll
-      for (int nb = 0; nb < NB; nb += 2) {
-        const int i = lane >> 3;
-        uint32_t bfr[4];
-        sh_ldsm4(ab + (nb * 8 + (i >> 1) * 8 + (lane & 7)) * SH_PITCH + kc + (i & 1) * 8, bfr);
-        sh_mma(acc[nb], af, bfr[0], bfr[1]);
-        sh_mma(acc[nb + 1], af, bfr[2], bfr[3]);
-      }
-    }
-  }
-  asm volatile("cp.async.wait_group 0;" ::: "memory");
-  __syncthreads();   // every warp is done with the staging buffers before the partials reuse them
-  const int g = lane >> 2, t = lane & 3;
-  constexpr int RP = R + 4;
-  if (kh == 1) {
-#pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      const int col = nb * 8 + 2 * t;
-      red[(rg * 16 + g) * RP + col] = acc[nb][0];
-      red[(rg * 16 + g) * RP + col + 1] = acc[nb][1];
-      red[(rg * 16 + g + 8) * RP + col] = acc[nb][2];
-      red[(rg * 16 + g + 8) * RP + col + 1] = acc[nb][3];
-    }
+  // each row's adapter (an invalid one reads pool row 0; rows past M take row M - 1's) and the block's distinct
+  // adapters in order of first appearance: one pass of the K loop per distinct adapter, each row kept from the
+  // pass of its own, so a row's bits never depend on the rows that share its block
+  if (warp == 0) {
+    int a = adapters[min(m0 + lane, M - 1) / row_len];
+    if (a < 0 || a >= pool_rows) a = 0;
+    row_adp[lane] = a;
+    const uint32_t peers = __match_any_sync(0xffffffffu, a);
+    const bool first = (__ffs(peers) - 1) == lane;
+    const uint32_t firsts = __ballot_sync(0xffffffffu, first);
+    if (first) set[__popc(firsts & ((1u << lane) - 1u))] = a;
+    if (lane == 0) set_size = __popc(firsts);
   }
   __syncthreads();
-  if (kh == 0) {
+  for (int d = 0; d < set_size; ++d) {
+    const int a = set[d];
+    const __nv_bfloat16* Aa = A + (size_t)a * R * K;
+
+    auto stage = [&](int kb, int buf) {
+      const int k0 = kb * SH_BK;
+      __nv_bfloat16* xd = xs + buf * SH_ROWS * SH_PITCH;
+      __nv_bfloat16* ad = as + buf * R * SH_PITCH;
+      for (int i = threadIdx.x; i < SH_ROWS * 16; i += SH_THREADS) {
+        const int r = i >> 4, c = i & 15;
+        const bool valid = m0 + r < M;
+        sh_cp16(xd + r * SH_PITCH + c * 8, x + (size_t)(valid ? m0 + r : 0) * K + k0 + c * 8, valid);
+      }
+      for (int i = threadIdx.x; i < R * 16; i += SH_THREADS) {
+        const int r = i >> 4, c = i & 15;
+        sh_cp16(ad + r * SH_PITCH + c * 8, Aa + (size_t)r * K + k0 + c * 8, true);
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+
+    float acc[NB][4];
 #pragma unroll
-    for (int nb = 0; nb < NB; ++nb) {
-      const int col = nb * 8 + 2 * t;
+    for (int i = 0; i < NB; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
+    // prologue: K steps 0 .. SH_STAGES - 2 in flight (an empty group where K runs out keeps the group count)
+    for (int st = 0; st < SH_STAGES - 1; ++st) {
+      if (st < nk) stage(st, st);
+      else asm volatile("cp.async.commit_group;" ::: "memory");
+    }
+    for (int kb = 0; kb < nk; ++kb) {
+      asm volatile("cp.async.wait_group %0;" ::"n"(SH_STAGES - 2) : "memory");   // step kb has landed
+      __syncthreads();   // ... for every thread; and every warp is done with step kb - 1, whose buffer refills now
+      if (kb + SH_STAGES - 1 < nk) stage(kb + SH_STAGES - 1, (kb + SH_STAGES - 1) % SH_STAGES);
+      else asm volatile("cp.async.commit_group;" ::: "memory");
+      const __nv_bfloat16* xb = xs + (kb % SH_STAGES) * SH_ROWS * SH_PITCH;
+      const __nv_bfloat16* ab = as + (kb % SH_STAGES) * R * SH_PITCH;
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int row = rg * 16 + g + 8 * hf;
-        if (m0 + row < M) {
-          const float v0 = acc[nb][2 * hf] + red[row * RP + col];
-          const float v1 = acc[nb][2 * hf + 1] + red[row * RP + col + 1];
-          *reinterpret_cast<uint32_t*>(mid + (size_t)(m0 + row) * R + col) = pack_bf2(v0, v1);
+      for (int kk = 0; kk < 4; ++kk) {
+        const int kc = kh * 64 + kk * 16;
+        uint32_t af[4];
+        sh_ldsm4(xb + (rg * 16 + (lane & 15)) * SH_PITCH + kc + (lane >> 4) * 8, af);
+#pragma unroll
+        for (int nb = 0; nb < NB; nb += 2) {
+          const int i = lane >> 3;
+          uint32_t bfr[4];
+          sh_ldsm4(ab + (nb * 8 + (i >> 1) * 8 + (lane & 7)) * SH_PITCH + kc + (i & 1) * 8, bfr);
+          sh_mma(acc[nb], af, bfr[0], bfr[1]);
+          sh_mma(acc[nb + 1], af, bfr[2], bfr[3]);
         }
       }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();   // every warp is done with the staging buffers before the partials reuse them
+    const int g = lane >> 2, t = lane & 3;
+    constexpr int RP = R + 4;
+    if (kh == 1) {
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        const int col = nb * 8 + 2 * t;
+        red[(rg * 16 + g) * RP + col] = acc[nb][0];
+        red[(rg * 16 + g) * RP + col + 1] = acc[nb][1];
+        red[(rg * 16 + g + 8) * RP + col] = acc[nb][2];
+        red[(rg * 16 + g + 8) * RP + col + 1] = acc[nb][3];
+      }
+    }
+    __syncthreads();
+    if (kh == 0) {
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        const int col = nb * 8 + 2 * t;
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int row = rg * 16 + g + 8 * hf;
+          if (m0 + row < M && row_adp[row] == a) {
+            const float v0 = acc[nb][2 * hf] + red[row * RP + col];
+            const float v1 = acc[nb][2 * hf + 1] + red[row * RP + col + 1];
+            *reinterpret_cast<uint32_t*>(mid + (size_t)(m0 + row) * R + col) = pack_bf2(v0, v1);
+          }
+        }
+      }
+    }
+    __syncthreads();   // the partials are read before the next pass stages into the same shared memory
   }
 }
 
@@ -702,16 +784,15 @@ extern "C" int jb_int4_dequant(const int32_t* words, const uint16_t* scales, con
 extern "C" int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* lora_a, int rank, int pool_rows,
                               const int32_t* adapters, int row_len, uint16_t* mid, void* stream) {
   JB_REQUIRE(x && lora_a && adapters && mid, "jb_lora_shrink: null pointer");
-  JB_REQUIRE(m > 0 && m % 16 == 0, "jb_lora_shrink: m %d must be a positive multiple of 16", m);
+  JB_REQUIRE(m > 0, "jb_lora_shrink: m %d must be positive", m);
   JB_REQUIRE(k > 0 && k % 64 == 0, "jb_lora_shrink: k %d must be a positive multiple of 64", k);
-  JB_REQUIRE(row_len > 0 && row_len % 16 == 0, "jb_lora_shrink: row_len %d must be a multiple of 16", row_len);
+  JB_REQUIRE(row_len > 0, "jb_lora_shrink: row_len %d must be positive", row_len);
   JB_REQUIRE(pool_rows > 0, "jb_lora_shrink: pool_rows %d", pool_rows);
-  dim3 grid(m / 16);
   auto xb = reinterpret_cast<const __nv_bfloat16*>(x);
   auto ab = reinterpret_cast<const __nv_bfloat16*>(lora_a);
   auto mb = reinterpret_cast<__nv_bfloat16*>(mid);
   cudaStream_t st = (cudaStream_t)stream;
-  if (row_len % w4::SH_ROWS == 0 && k % w4::SH_BK == 0) {
+  if (k % w4::SH_BK == 0) {
     switch (rank) {
       case 16: return w4::launch_shrink_staged<2>(xb, m, k, ab, pool_rows, adapters, row_len, mb, st);
       case 32: return w4::launch_shrink_staged<4>(xb, m, k, ab, pool_rows, adapters, row_len, mb, st);
@@ -720,6 +801,11 @@ extern "C" int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* l
       default: set_error("jb_lora_shrink: rank %d (16, 32, 48 or 64)", rank); return JB_EINVAL;
     }
   }
+  // k not a multiple of 128: blocks of 16 rows of one adapter
+  JB_REQUIRE(m % 16 == 0 && row_len % 16 == 0,
+             "jb_lora_shrink: with k %d (not a multiple of 128), m %d and row_len %d must be multiples of 16", k, m,
+             row_len);
+  dim3 grid(m / 16);
   switch (rank) {
     case 16: w4::lora_shrink_kernel<2><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
     case 32: w4::lora_shrink_kernel<4><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
@@ -753,12 +839,19 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
   if (lora) {
     JB_REQUIRE(lora_b && adapters, "jb_w4a16_lora: LoRA needs lora_b and adapters");
     JB_REQUIRE(rank % 16 == 0 && rank <= 64, "jb_w4a16_lora: rank %d (16, 32, 48 or 64)", rank);
-    JB_REQUIRE(row_len > 0 && row_len % 32 == 0 && (row_len % w4::HM == 0 || w4::HM % row_len == 0),
-               "jb_w4a16_lora: row_len %d must be a multiple of 32 that divides or is divided by 128", row_len);
-    const int n_adp = row_len >= w4::HM ? 1 : w4::HM / row_len;
-    JB_REQUIRE(n_adp * rank <= w4::MAX_EXPAND, "jb_w4a16_lora: %d adapters per tile x rank %d exceeds %d", n_adp,
-               rank, w4::MAX_EXPAND);
+    JB_REQUIRE(row_len > 0, "jb_w4a16_lora: row_len %d must be positive", row_len);
     JB_REQUIRE(pool_rows > 0, "jb_w4a16_lora: pool_rows %d", pool_rows);
+    if (row_len % w4::HM) {   // the gathered expand: one adapter set per 256-row tile, kept in shared memory
+      JB_REQUIRE(pool_rows <= 32 * w4::MASK_WORDS,
+                 "jb_w4a16_lora: %d pool rows; with rows of %d tokens (not a multiple of 128) at most %d", pool_rows,
+                 row_len, 32 * w4::MASK_WORDS);
+      JB_REQUIRE((m + w4::BM - 1) / w4::BM <= w4::MAX_MASK_TILES,
+                 "jb_w4a16_lora: m %d; with rows of %d tokens (not a multiple of 128) at most %d tokens", m, row_len,
+                 w4::MAX_MASK_TILES * w4::BM);
+    } else {
+      JB_REQUIRE((m + row_len - 1) / row_len <= w4::Layout::MAX_ROWS, "jb_w4a16_lora: more than %d rows",
+                 w4::Layout::MAX_ROWS);
+    }
   }
   CUtensorMap tx, tw, ts, tz, tm, tl;
   int st;
@@ -781,13 +874,11 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
     tz = ts;
   }
   if (lora) {
-    JB_REQUIRE((m + row_len - 1) / row_len <= w4::Layout::MAX_ROWS, "jb_w4a16_lora: more than %d rows",
-               w4::Layout::MAX_ROWS);
     JB_REQUIRE((reinterpret_cast<uintptr_t>(mid) & 15) == 0 && (reinterpret_cast<uintptr_t>(lora_b) & 15) == 0,
                "jb_w4a16_lora: mid and lora_b must be 16-byte aligned");
   }
   int planes3d = 0;
-  if (lora && row_len >= w4::HM) {
+  if (lora && row_len % w4::HM == 0) {
     // the planes maps; where the driver refuses them, 2D maps of one plane per load
     planes3d = make_tmap_planes(&tm, mid, m, rank, (uint64_t)rank * 2, w4::HM) == JB_OK &&
                make_tmap_planes(&tl, lora_b, (uint64_t)pool_rows * columns, rank, (uint64_t)rank * 2, w4::BN) == JB_OK;

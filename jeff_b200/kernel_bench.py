@@ -7,13 +7,20 @@ cfg1: one int4 W4A16 + LoRA product: M 64 tokens, K 1024, N 3584, one rank-16 ad
   scales and zeros. Algorithmic bytes per call 2,686,976 (words 1,835,008 + scales 57,344 + zeros 57,344 + x 131,072
   + y 458,752 + A 32,768 + B 114,688): HBM-bound. Timed as a CUDA graph of 256 calls cycling through enough distinct
   weight copies to exceed twice the 126 MB L2, so each call streams its weights from HBM.
+cfg2: the projection sweep over one decoder layer (q 1024->2048, k and v 1024->512, o 2048->1024, gate and up
+  1024->3584, down 3584->1024, q with its gate 1024->4096): 64 requests of 32 to 128 tokens packed into M = 4096 rows
+  with one adapter id per token, 8 rank-16 adapters, int4 group 128 with bf16 scales and zeros. Per projection
+  FLOPs 2MNK + 2M 16 (K + N) and algorithmic bytes K N / 2 + 2 (K / 128) N 2 + M K 2 + M N 2 + 8 16 (K + N) 2 + M 4:
+  tensor-bound (400 to 1500 FLOP per byte), so each line gives TFLOP/s against the measured bf16 peak beside GB/s.
+  Timed like cfg1, cycling through enough copies of x, the weights and y to exceed twice the L2.
 cfg3: one Gated DeltaNet prefill layer: 64 rows x 256 new tokens, each from a pooled fp32 state ~ N(0, 0.1). The
   prep kernel (conv width 4 + SiLU + L2 norms + gates from the projection output) reads 201 MB of q/k/v inputs,
   1 MB of gates and 2.4 MB of convolution tails and writes 201 MB of q/k/v and 1.5 MB of g/beta; the chunked scan
   reads q, k, v (201 MB), g and beta (1.5 MB) and the states (67 MB) and writes o (67 MB): 337 MB.
 
 One JSON line per kernel: milliseconds per call, GB/s of algorithmic bytes, and the fraction of the measured HBM copy
-bandwidth (MEASURED_PEAKS.json beside the repository root when present)."""
+bandwidth (MEASURED_PEAKS.json beside the repository root when present); for cfg2 also TFLOP/s and the fraction of
+the measured dense bf16 peak (the burst figure: each kernel is timed alone)."""
 
 from __future__ import annotations
 
@@ -37,6 +44,13 @@ def hbm_peak() -> tuple[float, str]:
     if p.exists():
         return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def tensor_peak() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"]), "measured"
+    return 1590.0, "fallback"
 
 
 def timed(fn, reps: int) -> float:
@@ -90,6 +104,54 @@ def cfg1(reps: int) -> dict:
             "ms": ms, "bytes": algo, "weight_copies": copies}
 
 
+def cfg2(reps: int) -> list[dict]:
+    lengths = synthetic.cfg2_lengths()
+    chosen = synthetic.cfg2_adapters()
+    per_token = torch.tensor(chosen, dtype=torch.int32).repeat_interleave(torch.tensor(lengths)).cuda()
+    m = sum(lengths)
+    lines = []
+    for name, k, n in synthetic.CFG2_SHAPES:
+        proj = synthetic.cfg2_projection(name, k, n)
+        packed = proj.packed
+        per_copy = m * k * 2 + packed.words.numel() * 4 + 2 * packed.scales.numel() * 2 + m * n * 2
+        copies = math.ceil(2 * L2_BYTES / per_copy)
+        dev = packed.to("cuda")
+        words = [kernels.int4_repack(dev.words.clone()) for _ in range(copies)]
+        scales = [dev.scales.clone() for _ in range(copies)]
+        zeros = [dev.zeros.clone() for _ in range(copies)]
+        xs = [proj.x.cuda() for _ in range(copies)]
+        ys = [torch.empty(m, n, dtype=torch.bfloat16, device="cuda") for _ in range(copies)]
+        a_pool, b_pool = proj.lora_a.cuda(), proj.lora_b.cuda()
+        mid = torch.empty(m, a_pool.shape[1], dtype=torch.bfloat16, device="cuda")
+        calls = 8 * copies
+
+        def body() -> None:
+            for i in range(calls):
+                j = i % copies
+                kernels.int4_product(xs[j], words[j], scales[j], zeros[j], packed.group, n, a_pool, b_pool,
+                                     per_token, 1, mid=mid, y=ys[j])
+
+        body()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            body()
+        ms = timed(graph.replay, reps) / calls
+        rank, n_adapters = a_pool.shape[1], a_pool.shape[0] - 1
+        flops = 2 * m * n * k + 2 * m * rank * (k + n)
+        algo = (k * n // 2 + 2 * (k // 128) * n * 2 + m * k * 2 + m * n * 2 + n_adapters * rank * (k + n) * 2
+                + m * 4)
+        lines.append({"kernel": "w4a16_lora (lora_shrink + w4a16_lora_kernel)",
+                      "config": f"cfg2 {name} M{m} K{k} N{n} packed 64 requests, 8 rank-16 adapters, g128z",
+                      "ms": ms, "bytes": algo, "flops": flops, "copies": copies})
+        del graph, words, scales, zeros, xs, ys
+        torch.cuda.empty_cache()
+    lines.append({"kernel": "cfg2 sweep: the 8 projections one after another", "config": "cfg2 M4096 packed",
+                  "ms": sum(x["ms"] for x in lines), "bytes": sum(x["bytes"] for x in lines),
+                  "flops": sum(x["flops"] for x in lines)})
+    return lines
+
+
 def cfg3(reps: int) -> list[dict]:
     rows, n = 64, 256
     t = rows * n
@@ -124,9 +186,13 @@ def main() -> None:
         raise SystemExit("kernel_bench needs a CUDA GPU")
     torch.cuda.set_device(0)
     peak, source = hbm_peak()
-    for line in [cfg1(args.reps), *cfg3(args.reps)]:
+    tpeak, tsource = tensor_peak()
+    for line in [cfg1(args.reps), *cfg2(args.reps), *cfg3(args.reps)]:
         gbs = line["bytes"] / (line["ms"] / 1e3) / 1e9
         line.update(gbs=gbs, hbm_peak_gbs=peak, peak_source=source, frac=gbs / peak)
+        if "flops" in line:
+            tflops = line["flops"] / (line["ms"] / 1e3) / 1e12
+            line.update(tflops=tflops, bf16_peak_tflops=tpeak, tensor_peak_source=tsource, tensor_frac=tflops / tpeak)
         print(json.dumps(line), flush=True)
 
 

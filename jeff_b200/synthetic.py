@@ -224,3 +224,58 @@ def make_cfg4_rows(seed: int, calls: int = 64, new_tokens: int = 128, prefix_tok
     new = torch.randint(0, vocab, (calls, new_tokens), generator=g).tolist()
     counts = torch.randint(2, 33, (calls,), generator=g).tolist()
     return PassRows(chosen, [prefix_of[a] for a in chosen], new, counts)
+
+
+# ---------------------------------------------------------------- configuration 2: the projection sweep
+
+# one decoder layer's projections (name, k, n): q/k/v/o, gate/up/down, and the attention input as the reference runs
+# it (q with its output gate, 1024 -> 4096)
+CFG2_SHAPES = (("q", 1024, 2048), ("k", 1024, 512), ("v", 1024, 512), ("o", 2048, 1024), ("gate", 1024, 3584),
+               ("up", 1024, 3584), ("down", 3584, 1024), ("q_gate", 1024, 4096))
+
+
+def cfg2_lengths(seed: int = 2, requests: int = 64, total: int = 4096, lo: int = 32, hi: int = 128) -> list[int]:
+    """The reference benchmark configuration 2's request lengths: `requests` draws from U{lo..hi}, then moved by one
+    token at a time, round robin over the requests and staying inside [lo, hi], until they sum to `total`."""
+    if not requests * lo <= total <= requests * hi:
+        raise ValueError(f"{requests} lengths in [{lo}, {hi}] cannot sum to {total}")
+    lengths = torch.randint(lo, hi + 1, (requests,), generator=generator(seed, "cfg2/lengths")).tolist()
+    i = 0
+    while (gap := total - sum(lengths)) != 0:
+        step = 1 if gap > 0 else -1
+        if lo <= lengths[i] + step <= hi:
+            lengths[i] += step
+        i = (i + 1) % requests
+    return lengths
+
+
+def cfg2_adapters(seed: int = 2, requests: int = 64, adapters: int = 8) -> list[int]:
+    """Each request's adapter: pool rows 1..adapters uniformly at random (row 0 is the base, no update)."""
+    return torch.randint(1, adapters + 1, (requests,), generator=generator(seed, "cfg2/adapters")).tolist()
+
+
+@dataclass
+class Cfg2Projection:
+    """One projection of the sweep: packed int4 weights (group 128 with bf16 scale and zero), the LoRA pools with
+    row 0 zeros and rows 1..8 rank-16 adapters (A ~ N(0, 0.02), B ~ N(0, 0.01) with alpha / r = 2 folded in), and
+    the packed pass's input x (tokens, k) ~ N(0, 1), bf16."""
+    name: str
+    k: int
+    n: int
+    packed: PackedInt4
+    W: torch.Tensor
+    lora_a: torch.Tensor     # (9, 16, k)
+    lora_b: torch.Tensor     # (9, columns, 16)
+    x: torch.Tensor
+
+
+def cfg2_projection(name: str, k: int, n: int, tokens: int = 4096, seed: int = 2, adapters: int = 8,
+                    rank: int = C.LORA_RANK, alpha: float = 32.0) -> Cfg2Projection:
+    w = normal(seed, f"cfg2/{name}/W", (n, k), 0.02)
+    packed, W = quantize_pack(w, "g128z")
+    lora_a = torch.zeros(adapters + 1, rank, k, dtype=DT)
+    lora_b = torch.zeros(adapters + 1, packed.columns, rank, dtype=DT)
+    lora_a[1:] = normal(seed, f"cfg2/{name}/A", (adapters, rank, k), 0.02).to(DT)
+    lora_b[1:, :n] = (normal(seed, f"cfg2/{name}/B", (adapters, n, rank), 0.01) * (alpha / rank)).to(DT)
+    x = normal(seed, f"cfg2/{name}/x", (tokens, k), 1.0).to(DT)
+    return Cfg2Projection(name, k, n, packed, W, lora_a, lora_b, x)

@@ -133,6 +133,8 @@ def exact_product(x: torch.Tensor, W: torch.Tensor, a_rows, b_rows, row_of: torc
     (96, 3584, [1024], 32),                       # down_proj, k = 3584
     (2048, 1024, [3584], 128),                    # many tiles per persistent CTA
     (384, 1024, [1024], 128),                     # a tile whose second 128-row half lies past m
+    (300, 1024, [2048], 1),                       # one adapter id per token: every adapter of the pool in a tile
+    (288, 2048, [1024, 512], 48),                 # rows of 48 tokens: tiles and halves that span rows
 ])
 def test_int4_lora_product_within_its_error_bound(fmt: str, m: int, k: int, outs: list[int], row_len: int) -> None:
     g = torch.Generator().manual_seed(m + k + len(outs))
@@ -199,6 +201,9 @@ def test_int4_lora_product_swiglu_epilogue(fmt: str) -> None:
     (256, 1024, 48, 32),      # staged, rows of 32 tokens
     (96, 1024, 32, 16),       # 16-row kernel: rows of 16 tokens
     (96, 960, 16, 32),        # 16-row kernel: K not a multiple of 128
+    (200, 1024, 16, 1),       # staged, one adapter id per token: blocks of several adapters
+    (240, 2048, 32, 48),      # staged, rows of 48 tokens: blocks that span two rows
+    (100, 1024, 64, 7),       # staged, rows of 7 tokens, m not a multiple of the block
 ])
 def test_lora_shrink_matches_the_oracle(m: int, k: int, rank: int, row_len: int) -> None:
     """mid = bf16(x A[a]^T) per row's adapter: within one bf16 step of the float32 product (summation order), and the
@@ -214,6 +219,61 @@ def test_lora_shrink_matches_the_oracle(m: int, k: int, rank: int, row_len: int)
     torch.testing.assert_close(got.float(), bf(want), rtol=BF16_STEP, atol=1e-6)
     again = kernels.lora_shrink(x.cuda(), a_pool.cuda(), adapters.cuda(), row_len).cpu()
     assert torch.equal(got, again)
+
+
+def test_lora_shrink_per_token_ids_give_the_bits_of_whole_rows() -> None:
+    """The shrink with one adapter id per token (blocks of several adapters, one K pass per adapter) returns the
+    same bits as with those tokens' rows of 64 (blocks of one adapter): a row's result depends on its own x and
+    adapter only."""
+    g = torch.Generator().manual_seed(11)
+    m, k, rank, row_len = 256, 1024, 16, 64
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+    a_pool = (torch.randn(4, rank, k, generator=g) * 0.02).to(torch.bfloat16).cuda()
+    rows = torch.tensor([3, 1, 1, 2], dtype=torch.int32)
+    whole = kernels.lora_shrink(x, a_pool, rows.cuda(), row_len)
+    per_token = kernels.lora_shrink(x, a_pool, rows.repeat_interleave(row_len).cuda(), 1)
+    assert np.array_equal(bits(whole), bits(per_token))
+
+
+# ---------------------------------------------------------------- configuration 2: packed requests of mixed lengths
+
+
+@pytest.fixture(scope="module")
+def cfg2_pass() -> tuple[list[int], list[int], torch.Tensor]:
+    lengths = synthetic.cfg2_lengths()
+    chosen = synthetic.cfg2_adapters()
+    per_token = torch.tensor(chosen, dtype=torch.int32).repeat_interleave(torch.tensor(lengths))
+    return lengths, chosen, per_token
+
+
+@pytest.mark.parametrize("shape", synthetic.CFG2_SHAPES, ids=[s[0] for s in synthetic.CFG2_SHAPES])
+def test_cfg2_packed_projection_within_its_bound_and_equal_to_the_padded_pass(cfg2_pass, shape) -> None:
+    """Configuration 2: 64 requests of 32 to 128 tokens packed into 4096 rows with one adapter id per token (row_len
+    1: the gathered expand over each tile's adapters, shrink blocks of several adapters), 8 rank-16 adapters, int4
+    group 128 with zeros. Every output lies within the error bound of the exact product (as above), and every row
+    is bit for bit the row of the same request padded to a 128-token row (row_len 128: one adapter per 128-row half,
+    the expand loaded by TMA): a row's bits depend on its own input and adapter only, however requests are laid
+    out in the pass."""
+    lengths, chosen, per_token = cfg2_pass
+    name, k, n = shape
+    proj = synthetic.cfg2_projection(name, k, n)
+    words = kernels.int4_repack(proj.packed.words.cuda())
+    scales, zeros = proj.packed.scales.cuda(), proj.packed.zeros.cuda()
+    a_pool, b_pool = proj.lora_a.cuda(), proj.lora_b.cuda()
+    got = kernels.int4_product(proj.x.cuda(), words, scales, zeros, proj.packed.group, n, a_pool, b_pool,
+                               per_token.cuda(), 1).cpu()
+    starts = np.cumsum([0, *lengths[:-1]]).tolist()
+    padded = torch.zeros(len(lengths) * 128, k, dtype=torch.bfloat16)
+    for i, (s0, ln) in enumerate(zip(starts, lengths, strict=True)):
+        padded[128 * i:128 * i + ln] = proj.x[s0:s0 + ln]
+    got_padded = kernels.int4_product(padded.cuda(), words, scales, zeros, proj.packed.group, n, a_pool, b_pool,
+                                      torch.tensor(chosen, dtype=torch.int32).cuda(), 128).cpu()
+    rows = torch.cat([torch.arange(128 * i, 128 * i + ln) for i, ln in enumerate(lengths)])
+    assert np.array_equal(bits(got), bits(got_padded[rows]))
+    exact, bound = exact_product(proj.x.float(), proj.W.float(), proj.lora_a.float(), proj.lora_b[:, :n].float(),
+                                 per_token.long())
+    err = (got.double() - exact).abs()
+    assert int((err > bound).sum()) == 0, f"worst at {(err / bound.clamp_min(1e-30)).max():.3g} x the bound"
 
 
 # ---------------------------------------------------------------- norms and activations
