@@ -357,16 +357,28 @@ __global__ void __launch_bounds__(THREADS, 1)
             *reinterpret_cast<uint4*>(wt + sw128_offset(n, r)) = dequant8(w[r], s2, zb2);
         } else if (!lora_tma) {
           // LoRA block, gathered: expand columns [col0, col0 + 64) of the tile's adapters in pool-row order, rank
-          // columns each. Row lrow of each half puts its mid in its adapter's block; weight column n holds each
-          // block's adapter's B row. Every global load of the block is issued before any store, so their
-          // latencies overlap.
+          // columns each. Weight column n holds each block's adapter's B row; row lrow of each half puts its mid
+          // in its adapter's block. The loads of each phase (B, then each half's mid) are issued before its stores,
+          // so their latencies overlap.
           const uint32_t* mask = s_mask + mt * MASK_WORDS;
           const int ke = mask_count(mask) * p.rank;    // expand columns of this tile
           const int col0 = (kb - nkb) * BK;
           const int lrow = n;
           const int gn = n0 + n;
-          uint4 xv[2][8], wv[8];
+          uint4 v[8];
 #pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const int col = col0 + 8 * c8;
+            v[c8] = make_uint4(0, 0, 0, 0);
+            if (col < ke && gn < p.columns) {
+              const int a = mask_nth(mask, col / p.rank);
+              v[c8] = *reinterpret_cast<const uint4*>(p.lora_b + ((size_t)a * p.columns + gn) * p.rank +
+                                                      (col % p.rank));
+            }
+          }
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) *reinterpret_cast<uint4*>(wt + sw128_offset(n, c8)) = v[c8];
+#pragma unroll 1
           for (int h = 0; h < 2; ++h) {
             const int gm = m0 + h * HM + lrow;
             int a = gm < p.M ? p.adapters[gm / p.row_len] : -1;
@@ -375,29 +387,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int c8 = 0; c8 < 8; ++c8) {
               const int col = col0 + 8 * c8;
-              xv[h][c8] = make_uint4(0, 0, 0, 0);
+              v[c8] = make_uint4(0, 0, 0, 0);
               if (a >= 0 && col >= lo && col < lo + p.rank)
-                xv[h][c8] = *reinterpret_cast<const uint4*>(p.mid + (size_t)gm * p.rank + (col - lo));
+                v[c8] = *reinterpret_cast<const uint4*>(p.mid + (size_t)gm * p.rank + (col - lo));
             }
-          }
-#pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) {
-            const int col = col0 + 8 * c8;
-            wv[c8] = make_uint4(0, 0, 0, 0);
-            if (col < ke && gn < p.columns) {
-              const int a = mask_nth(mask, col / p.rank);
-              wv[c8] = *reinterpret_cast<const uint4*>(p.lora_b + ((size_t)a * p.columns + gn) * p.rank +
-                                                       (col % p.rank));
-            }
-          }
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
             uint8_t* xt = smem + L::OFF_X + s * L::X_BYTES + h * (HM * 128);
 #pragma unroll
-            for (int c8 = 0; c8 < 8; ++c8) *reinterpret_cast<uint4*>(xt + sw128_offset(lrow, c8)) = xv[h][c8];
+            for (int c8 = 0; c8 < 8; ++c8) *reinterpret_cast<uint4*>(xt + sw128_offset(lrow, c8)) = v[c8];
           }
-#pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) *reinterpret_cast<uint4*>(wt + sw128_offset(n, c8)) = wv[c8];
         }
         fence_proxy_async_smem();
         __syncwarp();
@@ -584,7 +581,7 @@ __device__ __forceinline__ void sh_mma(float (&c)[4], const uint32_t (&a)[4], ui
 
 template <int NB>
 constexpr int shrink_staged_smem() {
-  return (SH_STAGES * SH_ROWS * SH_PITCH + SH_STAGES * NB * 8 * SH_PITCH) * 2;
+  return SH_STAGES * (SH_ROWS + NB * 8) * SH_PITCH * 2;
 }
 
 template <int NB>

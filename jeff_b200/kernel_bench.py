@@ -137,17 +137,29 @@ def cfg2(reps: int) -> list[dict]:
         with torch.cuda.graph(graph):
             body()
         ms = timed(graph.replay, reps) / calls
+
+        def shrinks() -> None:
+            for i in range(calls):
+                kernels.lora_shrink(xs[i % copies], a_pool, per_token, 1, out=mid)
+
+        shrinks()
+        torch.cuda.synchronize()
+        shrink_graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(shrink_graph):
+            shrinks()
+        shrink_ms = timed(shrink_graph.replay, reps) / calls
         rank, n_adapters = a_pool.shape[1], a_pool.shape[0] - 1
         flops = 2 * m * n * k + 2 * m * rank * (k + n)
         algo = (k * n // 2 + 2 * (k // 128) * n * 2 + m * k * 2 + m * n * 2 + n_adapters * rank * (k + n) * 2
                 + m * 4)
         lines.append({"kernel": "w4a16_lora (lora_shrink + w4a16_lora_kernel)",
                       "config": f"cfg2 {name} M{m} K{k} N{n} packed 64 requests, 8 rank-16 adapters, g128z",
-                      "ms": ms, "bytes": algo, "flops": flops, "copies": copies})
-        del graph, words, scales, zeros, xs, ys
+                      "ms": ms, "shrink_ms": shrink_ms, "bytes": algo, "flops": flops, "copies": copies})
+        del graph, shrink_graph, words, scales, zeros, xs, ys
         torch.cuda.empty_cache()
     lines.append({"kernel": "cfg2 sweep: the 8 projections one after another", "config": "cfg2 M4096 packed",
-                  "ms": sum(x["ms"] for x in lines), "bytes": sum(x["bytes"] for x in lines),
+                  "ms": sum(x["ms"] for x in lines), "shrink_ms": sum(x["shrink_ms"] for x in lines),
+                  "bytes": sum(x["bytes"] for x in lines),
                   "flops": sum(x["flops"] for x in lines)})
     return lines
 
