@@ -98,6 +98,12 @@ class BatchedPath:
         self.inp_host = torch.zeros(size, dtype=torch.int32).pin_memory()
         self.inp_np = self.inp_host.numpy()
         self.out_host = torch.zeros(max(C.BATCH_BUCKETS), C.READOUT_ROWS, dtype=torch.float32).pin_memory()
+        # decide()'s passes, enqueued back to back: a second pinned input buffer (the two alternate, so one is
+        # filled while the copy out of the other may still run), and pinned outputs and events per pass
+        self.inp_host2 = torch.zeros(size, dtype=torch.int32).pin_memory()
+        self.in_copied = [torch.cuda.Event(), torch.cuda.Event()]
+        self.pass_out: list[torch.Tensor] = []
+        self.pass_events: list[tuple[torch.cuda.Event, torch.cuda.Event]] = []
         psize = max((PREFIX_META + self._prefix_width(nb) + nb) * b for nb, cap in PREFIX_PASS_ROWS.items()
                     for b in C.BATCH_BUCKETS if b <= cap and b * nb <= max_tokens) if max_tokens >= 64 else 1
         self.prefix_inp = torch.zeros(psize, dtype=torch.int32, device=dev)
@@ -317,11 +323,14 @@ class BatchedPath:
 
     # ------------------------------------------------------------ requests
 
-    def fill(self, b: int, n: int, part: Sequence[tuple[int, int, Row]], lengths: Sequence[int]) -> int:
-        """Stage rows into the pinned input buffer (padding rows: slot 0, adapter 0, one token, one option)."""
+    def fill(self, b: int, n: int, part: Sequence[tuple[int, int, Row]], lengths: Sequence[int],
+             host: np.ndarray | None = None) -> int:
+        """Stage rows into a pinned input buffer (`host`, by default the first; padding rows: slot 0, adapter 0, one
+        token, one option)."""
+        host = self.inp_np if host is None else host
         size = C.META * b + b * n
-        meta = self.inp_np[:C.META * b].reshape(C.META, b)
-        ids = self.inp_np[C.META * b:size]
+        meta = host[:C.META * b].reshape(C.META, b)
+        ids = host[C.META * b:size]
         meta[:4] = 0
         meta[4] = 1
         ids[:] = 0
@@ -346,6 +355,40 @@ class BatchedPath:
         self.end.record(stream)
         self.end.synchronize()
         return self.out_host[:b].numpy(), self.start.elapsed_time(self.end)
+
+    def run_passes(self, passes: Sequence[tuple[int, int, Sequence[tuple[int, int, Row]], Sequence[int]]]
+                   ) -> list[tuple[np.ndarray, float]]:
+        """Several passes (b, n, rows, prefix lengths) enqueued back to back on the current stream, with one wait at
+        the end instead of one per pass: pass i's input is staged in pinned buffer i % 2 while pass i - 1 runs (after
+        the copy that last read that buffer is done), its probabilities come back into a pinned buffer of its own.
+        Every graph is recorded before the first pass is enqueued. Returns (probs (B, 255), ms) per pass, in order;
+        ms is the device time from the pass's input copy to its output copy."""
+        for b, n, _, _ in passes:
+            self.graph(b, n)
+        while len(self.pass_out) < len(passes):
+            self.pass_out.append(torch.zeros(max(C.BATCH_BUCKETS), C.READOUT_ROWS, dtype=torch.float32).pin_memory())
+            self.pass_events.append((torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)))
+        stream = torch.cuda.current_stream(self.device)
+        hosts = ((self.inp_host, self.inp_np), (self.inp_host2, self.inp_host2.numpy()))
+        for i, (b, n, part, lengths) in enumerate(passes):
+            graph, out = self.graph(b, n)
+            host, host_np = hosts[i % 2]
+            if i >= 2:
+                self.in_copied[i % 2].synchronize()
+            size = self.fill(b, n, part, lengths, host_np)
+            start, end = self.pass_events[i]
+            start.record(stream)
+            self.inp[:size].copy_(host[:size], non_blocking=True)
+            self.in_copied[i % 2].record(stream)
+            graph.replay()
+            self.pass_out[i][:b].copy_(out, non_blocking=True)
+            end.record(stream)
+        results = []
+        for i, (b, _, _, _) in enumerate(passes):
+            start, end = self.pass_events[i]
+            end.synchronize()
+            results.append((self.pass_out[i][:b].numpy(), start.elapsed_time(end)))
+        return results
 
     def _check(self, rows: Sequence[tuple[int, int, Row]]) -> list[int]:
         loaded = set(self.fast.adapter_index.values())
@@ -376,18 +419,20 @@ class BatchedPath:
         results: list[list[float]] = [[] for _ in rows]
         batch_rows, bucket, adapters_in_pass = [0] * len(rows), [0] * len(rows), [0] * len(rows)
         timing: dict[str, Any] = {"model_ms": 0.0, "new_tokens": sum(len(r.new_ids) for _, _, r in rows), "passes": 0}
+        plan: list[tuple[int, int, list[int]]] = []
         for n, members in sorted(by_bucket.items()):
             cap = min(max_rows(n), self.ws.rows, self.max_tokens // n)
             for first in range(0, len(members), cap):
                 part = members[first:first + cap]
-                b = next(bb for bb in C.BATCH_BUCKETS if bb >= len(part))
-                probs, ms = self.run_pass(b, n, [rows[i] for i in part], [lengths[i] for i in part])
-                timing["model_ms"] += ms
-                timing["passes"] += 1
-                adapters = len({rows[i][0] for i in part})
-                for j, i in enumerate(part):
-                    results[i] = probs[j, :rows[i][2].count].tolist()
-                    batch_rows[i], bucket[i], adapters_in_pass[i] = len(part), n, adapters
+                plan.append((next(bb for bb in C.BATCH_BUCKETS if bb >= len(part)), n, part))
+        done = self.run_passes([(b, n, [rows[i] for i in part], [lengths[i] for i in part]) for b, n, part in plan])
+        for (_, n, part), (probs, ms) in zip(plan, done, strict=True):
+            timing["model_ms"] += ms
+            timing["passes"] += 1
+            adapters = len({rows[i][0] for i in part})
+            for j, i in enumerate(part):
+                results[i] = probs[j, :rows[i][2].count].tolist()
+                batch_rows[i], bucket[i], adapters_in_pass[i] = len(part), n, adapters
         timing.update(batch_rows=batch_rows, bucket=bucket, adapters_in_pass=adapters_in_pass)
         tokens = [lengths[i] + len(row.new_ids) for i, (_, _, row) in enumerate(rows)]
         return results, tokens, timing

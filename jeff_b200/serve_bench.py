@@ -19,7 +19,8 @@ from its arrival to the end of the engine call that answered it. The reference's
 
 The run is open loop and single threaded per replica: arrival times are fixed in advance, and between engine calls
 the loop admits every call whose arrival time has passed, so a slow engine call makes the queue grow exactly as it
-would with independent clients. Before timing, every (adapter, prefix) pair of the stream is made resident (its
+would with independent clients. Each call is prepared (engine.prepare) before the clock starts, standing in for the
+reference's preparation threads, which prepare each request on arrival beside the GPU thread. Before timing, every (adapter, prefix) pair of the stream is made resident (its
 prefix pass run) and every decision graph recorded, so the timed runs see a warm pool (prefix misses are still
 counted). The run measures capacity first (a saturation stream: every call waiting at time 0), then replays an
 open-loop stream at `load` x capacity, and prints one JSON line: decisions/s, p50/p99 latency, batch sizes."""
@@ -130,8 +131,13 @@ class Served:
 
 
 def serve(engine, calls: Calls, window_ms: float = 1.0, max_batch_rows: int = 64,
-          clock: Callable[[], float] = time.perf_counter, sleep: Callable[[float], None] = time.sleep) -> Served:
-    """Answer `calls` (arrival-ordered) on `engine` with the micro-batching rule of the module docstring."""
+          clock: Callable[[], float] = time.perf_counter, sleep: Callable[[float], None] = time.sleep,
+          prepared: Sequence | None = None) -> Served:
+    """Answer `calls` (arrival-ordered) on `engine` with the micro-batching rule of the module docstring.
+    `prepared`: each call's engine.prepare() result, made beforehand, as the reference scheduler has its clients'
+    threads prepare each request on arrival (Scheduler.submit) while the GPU thread runs; a batch then joins its
+    calls' prepared rows per adapter (Prepared.join, as Scheduler._run does). Without it, rows are prepared on the
+    serving loop, inside the measured time."""
     n = len(calls)
     done = np.full(n, np.nan)
     queue: deque[int] = deque()
@@ -165,8 +171,12 @@ def serve(engine, calls: Calls, window_ms: float = 1.0, max_batch_rows: int = 64
         groups: dict[int, list[int]] = {}
         for i in batch:
             groups.setdefault(int(calls.adapter[i]), []).append(i)
-        work = [(adapter_id(a), engine.prepare(adapter_id(a), rows_of(calls, members)))
-                for a, members in groups.items()]
+        if prepared is not None:
+            work = [(adapter_id(a), type(prepared[members[0]]).join([prepared[i] for i in members]))
+                    for a, members in groups.items()]
+        else:
+            work = [(adapter_id(a), engine.prepare(adapter_id(a), rows_of(calls, members)))
+                    for a, members in groups.items()]
         results = engine.predict_many(work)
         finished = clock() - t0
         for (a, members), result in zip(groups.items(), results, strict=True):
@@ -261,8 +271,9 @@ def main() -> None:
 
     def run(calls: Calls) -> tuple[Served, Calls, float]:
         mine = calls.subset(route(calls.adapter, calls.prefix, world)[rank])
+        ready = [engine.prepare(adapter_id(int(mine.adapter[i])), rows_of(mine, [i])) for i in range(len(mine))]
         replicas.barrier(world)
-        served = serve(engine, mine, args.window_ms, args.max_batch_rows)
+        served = serve(engine, mine, args.window_ms, args.max_batch_rows, prepared=ready)
         return served, mine, replicas.max_over_ranks(served.elapsed, world)
 
     sat_served, sat_mine, sat_elapsed = run(saturation)

@@ -42,6 +42,7 @@ class FakeEngine:
         return rows
 
     def predict_many(self, groups):
+        groups = [(adapter, getattr(rows, "rows", rows)) for adapter, rows in groups]
         self.calls.append([(adapter, len(rows)) for adapter, rows in groups])
         self.clock.t += self.service_s
         return [FakeResult([[0.5, 0.5]] * len(rows), {"prefix_misses": 0, "passes": len(groups)})
@@ -115,3 +116,14 @@ def test_routing_keeps_each_binding_on_one_replica_and_spreads_them() -> None:
     bindings = np.bincount(list(owner.values()), minlength=8)
     assert bindings.min() > 0.6 * bindings.mean()
     assert sb.route(calls.adapter, calls.prefix, 1) == [list(range(len(calls)))]
+
+
+def test_prepared_calls_are_joined_per_adapter() -> None:
+    from jeff_b200.engine import Prepared
+
+    vc = VirtualClock()
+    engine = FakeEngine(vc, service_s=0.001)
+    calls = stream([0.0] * 5, adapters=[2, 1, 2, 2, 1])
+    ready = [Prepared([{"call": i}], [f"item {i}"], "fast", 7) for i in range(5)]
+    sb.serve(engine, calls, window_ms=1.0, clock=vc.clock, sleep=vc.sleep, prepared=ready)
+    assert engine.calls == [[("adapter-2", 3), ("adapter-1", 2)]]
