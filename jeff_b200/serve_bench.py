@@ -256,7 +256,7 @@ def main() -> None:
 
     from jeff_b200 import _lib, replicas
 
-    rank, world, _ = replicas.setup("nccl", timeout_s=900)
+    rank, world, _ = replicas.setup("nccl", timeout_s=300)
     _lib.load()
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but the launcher started {world} ranks")
