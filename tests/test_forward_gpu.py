@@ -10,7 +10,7 @@ Acceptance bar (the hot path's), held where it is meaningful:
   rounding points drifts apart from summation order alone (measured on the CPU: the oracle against itself with
   exact instead of float32 product sums moves probabilities by up to 9.4e-3 on this model; the GPU's chunked scan
   also rounds its state operands to bf16, as fla's chunk kernel that the reference runs does), so the chained pass is
-  judged on its outputs over all 64 calls: probabilities within 5e-2 and the chosen option identical on at least 56
+  checked on its outputs over all 64 calls: probabilities within 5e-2 and the chosen option identical on at least 56
   (these random-weight models give flat option distributions, where near-ties are common; the test prints the
   spread and the agreement)."""
 
@@ -128,7 +128,7 @@ def test_cfg4_layers_match_the_oracle_layer_by_layer(cfg4) -> None:
     every GPU layer runs on the oracle's input to that layer; its output residual stream (each row's 128 tokens x
     1024) is within 2e-2 of the oracle's (norm-wise). Chained through 24 layers, two bf16 implementations drift
     apart by more than that from summation order alone (the oracle against itself with exact instead of float32
-    product sums: 1.8% after 6 layers), so the chain is judged on its outputs (the next test)."""
+    product sums: 1.8% after 6 layers), so the chain is checked on its outputs (the next test)."""
     model, adapters, fast, path, rows, part, slots = cfg4
     picks = [0, 21, 42, 63]
     refs = oracle_rows(model, adapters, rows, picks)
