@@ -20,9 +20,9 @@ from its arrival to the end of the engine call that answered it. The reference's
 The run is open loop and single threaded per replica: arrival times are fixed in advance, and between engine calls
 the loop admits every call whose arrival time has passed, so a slow engine call makes the queue grow exactly as it
 would with independent clients. Each call is prepared (engine.prepare) before the clock starts, standing in for the
-reference's preparation threads, which prepare each request on arrival beside the GPU thread. Before timing, every (adapter, prefix) pair of the stream is made resident (its
-prefix pass run) and every decision graph recorded, so the timed runs see a warm pool (prefix misses are still
-counted). The run measures capacity first (a saturation stream: every call waiting at time 0), then replays an
+reference's preparation threads, which prepare each request on arrival beside the GPU thread. Before timing, every
+(adapter, prefix) pair of the stream is made resident (its prefix pass run) and every decision graph recorded, so
+the timed runs see a warm pool (prefix misses are still counted). The run measures capacity first (a saturation stream: every call waiting at time 0), then replays an
 open-loop stream at `load` x capacity, and prints one JSON line: decisions/s, p50/p99 latency, batch sizes."""
 
 from __future__ import annotations

@@ -15,7 +15,8 @@ def test_cfg2_lengths_fill_the_pass_inside_their_range() -> None:
     assert len(lengths) == 64 and sum(lengths) == 4096
     assert min(lengths) >= 32 and max(lengths) <= 128
     assert lengths == synthetic.cfg2_lengths()
-    assert sum(synthetic.cfg2_lengths(total=64 * 128)) == 64 * 128 and set(synthetic.cfg2_lengths(total=64 * 32)) == {32}
+    assert sum(synthetic.cfg2_lengths(total=64 * 128)) == 64 * 128
+    assert set(synthetic.cfg2_lengths(total=64 * 32)) == {32}
     with pytest.raises(ValueError, match="cannot sum"):
         synthetic.cfg2_lengths(total=64 * 128 + 1)
 
