@@ -22,6 +22,7 @@ from jeff_b200.prefix_pool import PrefixPool, pool_pages
 from jeff_b200.synthetic import AdapterWeights, FusedGroup, ModelWeights
 
 DT = torch.bfloat16
+MAX_ADAPTERS = 255   # pool rows (adapters + the base's row 0) the product's gathered LoRA expand can hold: 256
 
 
 def swiglu_order(inter: int, block: int = 64) -> torch.Tensor:
@@ -96,6 +97,9 @@ class FastPath:
                  base_readout: tuple[torch.Tensor, float] | None = None) -> None:
         if max_adapters < 1:
             raise ValueError(f"max_adapters={max_adapters}: the fast path needs room for at least one adapter")
+        if max_adapters > MAX_ADAPTERS:
+            raise ValueError(f"max_adapters={max_adapters}: the fast path holds at most {MAX_ADAPTERS} adapters (the "
+                             "product gathers a pass's LoRA updates from at most 256 pool rows, the base's included)")
         self.device = torch.device(device)
         self.model = model
         self.max_adapters = max_adapters

@@ -202,3 +202,12 @@ def test_decision_step_checks_and_abstains() -> None:
     assert make_decision([0.5, 0.5], 0.8).value == 0   # a tie takes the first option
     probs = torch.softmax(torch.randn(7, generator=torch.Generator().manual_seed(1)), 0).tolist()
     assert make_decision(probs, 0.8).value == max(range(7), key=probs.__getitem__)
+
+
+def test_the_fast_path_refuses_more_adapters_than_the_product_gathers() -> None:
+    from jeff_b200.fast_path import MAX_ADAPTERS, FastPath
+
+    with pytest.raises(ValueError, match="at most 255 adapters"):
+        FastPath(None, max_adapters=MAX_ADAPTERS + 1)   # type: ignore[arg-type]
+    with pytest.raises(ValueError, match="at least one adapter"):
+        FastPath(None, max_adapters=0)   # type: ignore[arg-type]
