@@ -183,6 +183,18 @@ class FastPath:
     def weight_bytes(self) -> int:
         return sum(lin.nbytes() for lin in self.lins)
 
+    def adapter_tensors(self, index: int) -> list[torch.Tensor]:
+        """The device memory of one adapter row, as views in a fixed order: every group's LoRA A and B rows, its
+        readout rows and its temperature (what an adapter add changes, so what the replicas re-broadcast)."""
+        if not 0 <= index <= self.max_adapters:
+            raise ValueError(f"Adapter row {index} is outside the pools' rows 0..{self.max_adapters}")
+        out = [self.readout_pool[index], self.temp_pool[index:index + 1]]
+        for lin in self.lins:
+            if lin.rank:
+                assert lin.lora_a is not None and lin.lora_b is not None
+                out += [lin.lora_a[index], lin.lora_b[index]]
+        return out
+
     def tensors(self) -> list[torch.Tensor]:
         """Every device tensor of the weights and adapter pools, in a fixed order (the NCCL broadcast at load)."""
         out = [self.embed, self.final_w1, self.readout_pool, self.temp_pool, self.inv_freq]

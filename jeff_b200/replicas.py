@@ -2,9 +2,10 @@
 
 Requests are independent (the reference's engine/batched_path.py:5-7), so each GPU holds the full int4 base, every
 adapter and its own prefix pool, and serves its own share of the calls; nothing crosses GPUs on the per-call path.
-What does cross them, once at load and again on every adapter add or remove: rank 0's weights and adapter pool
-rows, broadcast (NCCL over NVLink on the GPU box, gloo on the CPU for tests) into the other ranks' tensors of the
-same shapes, in one fixed order (FastPath.tensors()). Timing across ranks is the maximum over ranks.
+What does cross them: once at load, rank 0's weights and adapter pool rows, broadcast (NCCL over NVLink on the GPU
+box, gloo on the CPU for tests) into the other ranks' tensors of the same shapes, in one fixed order
+(FastPath.tensors()); on each adapter add, that adapter's row only (FastPath.adapter_tensors(row)); on a remove,
+nothing. Timing across ranks is the maximum over ranks.
 
 The process group is given a short timeout, so ranks that wait on a rank that died end with an error instead of
 waiting for good."""
@@ -62,6 +63,46 @@ def broadcast_tensors(tensors: Sequence[torch.Tensor], src: int = 0) -> None:
     check_same_layout(tensors)
     for t in tensors:
         dist.broadcast(t, src)
+
+
+def add_adapter_everywhere(fast, adapter, src: int = 0) -> int:
+    """Add an adapter on every rank at once: each rank packs it into its lowest free row (the same row everywhere,
+    since every rank adds and removes the same adapters in the same order), ranks other than `src` may pass a
+    skeleton of the same shapes (synthetic.make_adapter(..., skeleton=True)), and `src`'s row is then broadcast
+    into the others: the row's LoRA A and B of every group, its readout rows and temperature, and nothing else.
+    Returns the row. Every rank must call this, in the same order."""
+    import torch.distributed as dist
+
+    # a rank whose own add fails still joins the gather, so no rank is left waiting in a collective
+    try:
+        index, failure = fast.add_adapter(adapter), None
+    except Exception as error:  # noqa: BLE001 - reported to every rank below
+        index, failure = None, f"{type(error).__name__}: {error}"
+    outcomes: list = [None] * dist.get_world_size()
+    dist.all_gather_object(outcomes, (index, failure))
+    rows = [row for row, _ in outcomes]
+    if len(set(rows)) != 1 or rows[0] is None:
+        if index is not None:
+            fast.remove_adapter(adapter.name)
+        problems = "; ".join(f"rank {r}: {why}" for r, (_, why) in enumerate(outcomes) if why)
+        raise RuntimeError(f"The ranks put adapter {adapter.name} in different rows {rows}"
+                           f"{' (' + problems + ')' if problems else ''}; their adapter pools have drifted apart "
+                           "(add and remove the same adapters on every rank, in the same order)")
+    broadcast_tensors(fast.adapter_tensors(index), src)
+    return index
+
+
+def remove_adapter_everywhere(fast, name: str) -> None:
+    """Remove an adapter on every rank (no data moves: the row is freed and its cached prefixes forgotten on each
+    rank); every rank must call this, in the same order."""
+    fast.remove_adapter(name)
+    barrier(_size())
+
+
+def _size() -> int:
+    import torch.distributed as dist
+
+    return dist.get_world_size() if dist.is_initialized() else 1
 
 
 def barrier(size: int) -> None:

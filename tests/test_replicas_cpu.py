@@ -120,3 +120,117 @@ def test_two_gloo_ranks_broadcast_weights_and_reduce_times(mode: str) -> None:
         messages.append(errors.get())
     assert not messages, "\n".join(messages)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+
+
+class RowPools:
+    """FastPath's adapter rows on the CPU (FastPath itself needs the GPU): lowest-free-row placement as
+    FastPath.add_adapter does it, and FastPath.adapter_tensors' row views over pools of the same kinds."""
+
+    def __init__(self, max_adapters: int = 3) -> None:
+        import bisect  # noqa: F401
+
+        rows = max_adapters + 1
+        self.max_adapters = max_adapters
+        self.readout_pool = torch.zeros(rows, 8, 32, dtype=torch.bfloat16)
+        self.temp_pool = torch.ones(rows)
+        self.lins = [SimpleLin(rows, 16, 32, 64), SimpleLin(rows, 0, 32, 64), SimpleLin(rows, 32, 64, 32)]
+        self.free_rows = list(range(1, rows))
+        self.adapter_index: dict[str, int] = {}
+
+    def add_adapter(self, adapter) -> int:
+        index = self.free_rows.pop(0)
+        for lin, (a, b) in zip((x for x in self.lins if x.rank), adapter.lora, strict=True):
+            lin.lora_a[index].copy_(a)
+            lin.lora_b[index].copy_(b)
+        self.readout_pool[index].copy_(adapter.readout)
+        self.temp_pool[index] = adapter.temperature
+        self.adapter_index[adapter.name] = index
+        return index
+
+    def remove_adapter(self, name: str) -> None:
+        import bisect
+
+        bisect.insort(self.free_rows, self.adapter_index.pop(name))
+
+    def adapter_tensors(self, index: int) -> list[torch.Tensor]:
+        from jeff_b200.fast_path import FastPath
+
+        return FastPath.adapter_tensors(self, index)   # the real method over these pools
+
+
+class SimpleLin:
+    def __init__(self, rows: int, rank: int, k: int, columns: int) -> None:
+        self.rank = rank
+        self.lora_a = torch.zeros(rows, rank, k, dtype=torch.bfloat16) if rank else None
+        self.lora_b = torch.zeros(rows, columns, rank, dtype=torch.bfloat16) if rank else None
+
+
+def small_adapter(name: str, seed: int, skeleton: bool):
+    from types import SimpleNamespace
+
+    g = torch.Generator().manual_seed(seed)
+
+    def draw(*shape):
+        return torch.zeros(*shape, dtype=torch.bfloat16) if skeleton else torch.randn(*shape, generator=g).to(
+            torch.bfloat16)
+
+    return SimpleNamespace(name=name, lora=[(draw(16, 32), draw(64, 16)), (draw(32, 64), draw(32, 32))],
+                           readout=draw(8, 32), temperature=1.0 if skeleton else 0.5 + seed / 10)
+
+
+def _adapter_rank_main(rank: int, port: int, errors) -> None:
+    try:
+        sys.path.insert(0, str(ROOT))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2",
+                          LOCAL_RANK=str(rank))
+        import torch.distributed as dist
+
+        from jeff_b200 import replicas
+
+        replicas.setup("gloo", timeout_s=60)
+        pools = RowPools()
+        skeleton = rank != 0
+        assert replicas.add_adapter_everywhere(pools, small_adapter("a", 1, skeleton)) == 1
+        assert replicas.add_adapter_everywhere(pools, small_adapter("b", 2, skeleton)) == 2
+        replicas.remove_adapter_everywhere(pools, "a")
+        assert replicas.add_adapter_everywhere(pools, small_adapter("c", 3, skeleton)) == 1
+        want = RowPools()
+        want.add_adapter(small_adapter("c", 3, False))
+        want.add_adapter(small_adapter("b", 2, False))
+        for row in (1, 2):
+            for got, exp in zip(pools.adapter_tensors(row), want.adapter_tensors(row), strict=True):
+                assert torch.equal(got, exp), f"rank {rank} row {row}"
+        # pools that drifted apart (rank 1 holds an extra adapter) are refused on both ranks
+        if rank == 1:
+            pools.add_adapter(small_adapter("local", 9, False))
+        try:
+            replicas.add_adapter_everywhere(pools, small_adapter("d", 4, skeleton))
+            raise AssertionError("drifted pools were not refused")
+        except RuntimeError as error:
+            assert "different rows" in str(error)
+        assert "d" not in pools.adapter_index
+        replicas.barrier(2)
+        dist.destroy_process_group()
+    except BaseException:
+        errors.put(f"rank {rank}: {traceback.format_exc()}")
+        raise
+
+
+def test_two_gloo_ranks_add_and_remove_adapters_by_row() -> None:
+    ctx = mp.get_context("spawn")
+    errors = ctx.SimpleQueue()
+    port = _free_port()
+    procs = [ctx.Process(target=_adapter_rank_main, args=(r, port, errors)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+            p.join()
+    messages = []
+    while not errors.empty():
+        messages.append(errors.get())
+    assert not messages, "\n".join(messages)
+    assert all(p.exitcode == 0 for p in procs)
