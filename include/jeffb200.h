@@ -36,6 +36,12 @@ const char* jb_last_error(void);
  * Synchronises `stream`. Not for use inside graph capture. */
 int jb_device_status(int* status, int reset, void* stream);
 
+/* The product kernel's stage trace: out (16 x 256 uint64) receives clock64() stamps of CTA 0's hand-offs for its
+ * first 256 K blocks in the last launch (event rows as described in csrc/w4a16_gemm.cu). Only a library built with
+ * -DJB_TRACE (libjeffb200_trace.so) records them; the product library returns JB_EINVAL. A measurement aid with no
+ * reference counterpart. */
+int jb_stage_trace_read(uint64_t* out);
+
 /* ---------------------------------------------------------------- int4 W4A16 + multi-LoRA products (S1) */
 
 /* The reference's kernel word layout (int32 (k/8, columns); input 8i + j of column c in bits 4j..4j+3 of word

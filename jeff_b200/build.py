@@ -1,9 +1,11 @@
 """Builds libjeffb200.so in-tree (jeff_b200/libjeffb200.so) with nvcc for sm_100a.
 
-    python -m jeff_b200.build [--verbose]
+    python -m jeff_b200.build [--verbose] [--trace]
 
 One translation unit (csrc/lib.cu includes the kernel files), the CUDA runtime linked statically, so the library
-loads anywhere the driver exists (and, without a GPU, still loads and exports its symbols)."""
+loads anywhere the driver exists (and, without a GPU, still loads and exports its symbols). --trace builds
+libjeffb200_trace.so beside it, with the product kernel's stage trace compiled in (-DJB_TRACE; jeff_b200.stage_trace
+reads it); the library the package loads is always the one without."""
 
 from __future__ import annotations
 
@@ -17,6 +19,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 SRC = HERE / "csrc"
 LIB = HERE / "libjeffb200.so"
+TRACE_LIB = HERE / "libjeffb200_trace.so"
 INCLUDE = HERE.parent / "include"
 
 
@@ -31,19 +34,20 @@ def sources() -> list[Path]:
     return sorted(SRC.glob("*.cu")) + sorted(SRC.glob("*.cuh")) + sorted(INCLUDE.glob("*.h"))
 
 
-def up_to_date() -> bool:
-    if not LIB.exists():
+def up_to_date(lib: Path = LIB) -> bool:
+    if not lib.exists():
         return False
-    built = LIB.stat().st_mtime
+    built = lib.stat().st_mtime
     return all(p.stat().st_mtime <= built for p in sources())
 
 
-def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
-    if not force and up_to_date():
-        return LIB
+def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False, trace: bool = False) -> Path:
+    lib = TRACE_LIB if trace else LIB
+    if not force and up_to_date(lib):
+        return lib
     cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
-           "-shared", "-Xcompiler", "-fPIC", "-cudart", "static",
-           f"-I{INCLUDE}", "-o", str(LIB) + ".tmp", str(SRC / "lib.cu")]
+           "-shared", "-Xcompiler", "-fPIC", "-cudart", "static", *(["-DJB_TRACE"] if trace else []),
+           f"-I{INCLUDE}", "-o", str(lib) + ".tmp", str(SRC / "lib.cu")]
     if ptxas_info:
         cmd.insert(1, "-Xptxas=-v")
     if verbose:
@@ -53,8 +57,8 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose or ptxas_info:
         print(res.stderr, file=sys.stderr)
-    os.replace(str(LIB) + ".tmp", LIB)
-    return LIB
+    os.replace(str(lib) + ".tmp", lib)
+    return lib
 
 
 def main() -> None:
@@ -62,8 +66,9 @@ def main() -> None:
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-info", action="store_true")
+    ap.add_argument("--trace", action="store_true")
     args = ap.parse_args()
-    print(build(force=args.force, verbose=args.verbose, ptxas_info=args.ptxas_info))
+    print(build(force=args.force, verbose=args.verbose, ptxas_info=args.ptxas_info, trace=args.trace))
 
 
 if __name__ == "__main__":

@@ -36,6 +36,24 @@
 namespace jb {
 namespace w4 {
 
+// Stage trace (built only with -DJB_TRACE, `python -m jeff_b200.build --trace`): CTA 0 stamps clock64() at every
+// hand-off of its first 256 K blocks into g_stage_trace[event][k block]: 0 producer saw the stage free, 1 its TMA
+// loads issued, 2 / 3 the first warp of the K block's dequantiser group saw it full / arrived dequantised, 4 the
+// MMA thread's waits returned, 5 its MMAs and commit issued, 6 / 7 the epilogue started / finished tile `it`, 8..11
+// each dequantiser warp arrived, 12..15 each dequantiser warp saw the stage full. jb_stage_trace_read copies it out.
+// Without JB_TRACE the stamps compile to nothing.
+#ifdef JB_TRACE
+__device__ unsigned long long g_stage_trace[16][256];
+#define JB_STAGE(ev, kg)                                                                   \
+  do {                                                                                     \
+    if (blockIdx.x == 0 && (unsigned)(kg) < 256u) g_stage_trace[ev][kg] = clock64();       \
+  } while (0)
+#else
+#define JB_STAGE(ev, kg) \
+  do {                   \
+  } while (0)
+#endif
+
 constexpr int BM = 256;             // rows per tile (two UMMA halves of 128)
 constexpr int HM = 128;             // rows per half
 constexpr int BN = 128;
@@ -244,12 +262,14 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int kb = 0; kb < nkt; ++kb, ++kg) {
           const int s = kg % STAGES;
           if (!mbar_wait(&empty[s], ((kg / STAGES) & 1) ^ 1, abort_flag, p.err, 1)) break;
+          JB_STAGE(0, kg);
           if (kb < nkb) {
             mbar_arrive_expect_tx(&full[s], bytes);
             tma_load_2d(smem + L::OFF_X + s * L::X_BYTES, &tm_x, &full[s], kb * BK, m0);
             tma_load_2d(smem + L::OFF_RAW + s * L::RAW_BYTES, &tm_w, &full[s], n0, kb * (BK / 8));
             tma_load_2d(smem + L::OFF_SC + s * L::SC_BYTES, &tm_s, &full[s], n0, (kb * BK) / p.group);
             if (ZERO) tma_load_2d(smem + L::OFF_ZR + s * L::SC_BYTES, &tm_z, &full[s], n0, (kb * BK) / p.group);
+            JB_STAGE(1, kg);
           } else if (lora_tma) {
             // a LoRA block by TMA: for each of its halves, the half's mid rows (rank / 8 planes of 128 rows x 16 B)
             // into the x slot and its adapter's B rows for this column tile into the weight slot. Rows past m and
@@ -298,6 +318,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           const uint32_t ph = (kg / STAGES) & 1;
           ok = mbar_wait(&full[s], ph, abort_flag, p.err, 3) && mbar_wait(&deq[s], ph, abort_flag, p.err, 4);
           if (!ok) break;
+          JB_STAGE(4, kg);
           tc_fence_after();
           if (kb >= nkb && lora_tma) {
             // each half against its own adapter, planes layout: K16 step j reads planes 2j, 2j + 1
@@ -320,6 +341,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
           }
           tc_commit(&empty[s]);
+          JB_STAGE(5, kg);
         }
         if (!ok) break;
         tc_commit(&tmem_full[b]);
@@ -340,6 +362,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         if ((int)(kg % GROUPS) != grp) continue;
         const int s = kg % STAGES;
         ok = mbar_wait(&full[s], (kg / STAGES) & 1, abort_flag, p.err, 5);
+        if ((et & 127) == 0) JB_STAGE(2, kg);
+        if (lane == 0) JB_STAGE(12 + ((et >> 5) & 3), kg);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         uint8_t* wt = smem + L::OFF_W + s * L::W_BYTES;
         if (kb < nkb) {
@@ -399,6 +423,8 @@ __global__ void __launch_bounds__(THREADS, 1)
         fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&deq[s]);
+        if ((et & 127) == 0) JB_STAGE(3, kg);
+        if (lane == 0) JB_STAGE(8 + ((et >> 5) & 3), kg);
       }
     }
   } else {
@@ -415,6 +441,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (et == 0) *epi_ok = mbar_wait(&tmem_full[b], (it >> 1) & 1, abort_flag, p.err, 6) ? 1 : 0;
       named_barrier(2, EPI_WARPS * 32);
       if (!*epi_ok) break;
+      if (et == 0) JB_STAGE(6, it);
       tc_fence_after();
       const uint32_t acc = tmem + b * 2 * BN + lane_bits;
 #pragma unroll 1
@@ -477,6 +504,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tmem_empty[b]);
+      if (et == 0) JB_STAGE(7, it);
     }
   }
 
@@ -898,6 +926,18 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
                reinterpret_cast<__nv_bfloat16*>(y), ldy, device_status_word(), planes3d};
   if (zeros) return w4::launch<true>(tx, tw, ts, tz, tm, tl, p, (cudaStream_t)stream);
   return w4::launch<false>(tx, tw, ts, tz, tm, tl, p, (cudaStream_t)stream);
+}
+
+extern "C" int jb_stage_trace_read(uint64_t* out) {
+  JB_REQUIRE(out, "jb_stage_trace_read: null pointer");
+#ifdef JB_TRACE
+  return status_of(cudaMemcpyFromSymbol(out, w4::g_stage_trace, sizeof(w4::g_stage_trace)),
+                   "jb_stage_trace_read: copy");
+#else
+  set_error("jb_stage_trace_read: this library was built without the stage trace (python -m jeff_b200.build "
+            "--trace builds libjeffb200_trace.so with it)");
+  return JB_EINVAL;
+#endif
 }
 
 extern "C" int jb_int4_repack(const int32_t* words, int32_t* out, int k, int columns, void* stream) {
