@@ -216,6 +216,7 @@ class BatchedPath:
     # ------------------------------------------------------------ graphs
 
     def _capture(self, work: Callable[[], Any]) -> tuple[torch.cuda.CUDAGraph, Any]:
+        self.pool.sync()   # block tables current before capture (the captured pass only reads them)
         self.stream.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(self.stream):
             for _ in range(2):
@@ -328,6 +329,7 @@ class BatchedPath:
         """Stage rows into a pinned input buffer (`host`, by default the first; padding rows: slot 0, adapter 0, one
         token, one option)."""
         host = self.inp_np if host is None else host
+        self.pool.sync()   # the pass reads the block tables of every reservation made before it
         size = C.META * b + b * n
         meta = host[:C.META * b].reshape(C.META, b)
         ids = host[C.META * b:size]
@@ -453,6 +455,7 @@ class BatchedPath:
 
     def _prefix_pass(self, b: int, nb: int, part: Sequence[tuple[int, int, list[int]]]) -> float:
         graph = self.prefix_graph(b, nb)
+        self.pool.sync()
         w = self._prefix_width(nb)
         size = (PREFIX_META + w + nb) * b
         meta = self.prefix_inp_np[:PREFIX_META * b].reshape(PREFIX_META, b)
@@ -478,77 +481,86 @@ class BatchedPath:
         return self.start.elapsed_time(self.end)
 
     def ensure_prefixes(self, rows: Sequence[tuple[int, str]], max_tokens: int) -> tuple[list[int], dict[str, Any]]:
-        """Each row's prefix slot, pinned once per row (the caller unpins), processing missing prefixes in batched
-        prefix passes (batched_path.py:613-698); on failure every pin of the call is undone and unwritten
-        reservations are released."""
+        """Each row's prefix slot (adapter row, prefix text), pinned once per row (the caller unpins the list), with
+        the prefixes not yet in the pool processed by batched prefix passes (the reference's ensure_prefixes,
+        batched_path.py:613-698, same checks, messages and timing keys). All or nothing: if anything fails, every pin
+        taken here is returned and every reservation whose prefix pass did not run is released."""
         pool = self.pool
         loaded = set(self.fast.adapter_index.values())
-        keys = [(adapter, text) for adapter, text in rows]
-        for i, (adapter, _) in enumerate(keys):
-            if adapter not in loaded:
-                raise ValueError(f"Row {i}: adapter row {adapter} holds no loaded adapter (loaded rows: "
-                                 f"{sorted(loaded)})")
-        new_ids: dict[tuple[int, str], list[int]] = {}
-        for adapter, text in keys:
-            if (adapter, text) in new_ids or pool.lookup(adapter, text) is not None:
+        bad = next((i for i, (adapter, _) in enumerate(rows) if adapter not in loaded), None)
+        if bad is not None:
+            raise ValueError(f"Row {bad}: adapter row {rows[bad][0]} holds no loaded adapter (loaded rows: "
+                             f"{sorted(loaded)})")
+        # distinct keys in first-appearance order, each with the rows that use it
+        users: dict[tuple[int, str], list[int]] = {}
+        for i, key in enumerate(rows):
+            users.setdefault(tuple(key), []).append(i)          # type: ignore[arg-type]
+        cached = {key: slot for key in users if (slot := pool.lookup(*key)) is not None}
+        tokens: dict[tuple[int, str], list[int]] = {}
+        for key in users:
+            if key in cached:
                 continue
             if self.tokenize is None:
                 raise ValueError("This batched path has no tokenizer to process new prefixes")
-            ids = list(self.tokenize(text))
+            ids = list(self.tokenize(key[1]))
             if len(ids) > C.LONGEST_PREFIX_TOKENS:
                 raise ValueError(f"The question's fixed part has {len(ids)} tokens; the fast path holds at most "
                                  f"{C.LONGEST_PREFIX_TOKENS}")
             if len(ids) >= max_tokens:
                 raise ValueError(f"Question branch exceeds the {max_tokens}-token limit; no input was truncated.")
-            new_ids[(adapter, text)] = ids
-        timing: dict[str, Any] = {"prefix_ms": 0.0, "prefix_misses": len(new_ids), "prefix_hits": 0,
-                                  "prefix_shared": sum(1 for key in keys if key in new_ids) - len(new_ids),
-                                  "prefix_passes": 0}
-        pinned: list[int] = []
-        found: dict[tuple[int, str], int] = {}
-        reserved: dict[tuple[int, str], int] = {}
-        written: set[int] = set()
-        try:
-            for key in keys:
-                if key in new_ids:
-                    continue
-                timing["prefix_hits"] += 1
-                if key not in found:
-                    slot = pool.lookup(*key)
-                    if slot is None:
-                        raise RuntimeError(f"Prefix of adapter row {key[0]} left the pool before any reservation")
-                    pool.pin([slot])
-                    pinned.append(slot)
-                    found[key] = slot
-            for key, ids in new_ids.items():
-                slot = pool.reserve(key[0], key[1], len(ids))
-                reserved[key] = slot
-                pool.pin([slot])
-                pinned.append(slot)
-            slots = [found[key] if key in found else reserved[key] for key in keys]
-            again, seen = [], set()
-            for slot in slots:
-                if slot in seen:
-                    again.append(slot)
-                seen.add(slot)
-            pool.pin(again)
-            pinned.extend(again)
-            by_bucket: dict[int, list[tuple[int, str]]] = {}
-            for key, ids in new_ids.items():
-                nb = next(nb for nb in C.PREFIX_BUCKETS if nb >= max(len(ids), 1))
-                by_bucket.setdefault(nb, []).append(key)
-            for nb, members in sorted(by_bucket.items()):
-                first = 0
-                for b in self.prefix_passes(nb, len(members)):
-                    part = members[first:first + b]
-                    first += b
-                    timing["prefix_ms"] += self._prefix_pass(b, nb, [(reserved[k], k[0], new_ids[k]) for k in part])
+            tokens[key] = ids
+        timing: dict[str, Any] = dict(prefix_ms=0.0, prefix_misses=len(tokens),
+                                      prefix_hits=sum(len(users[k]) for k in cached),
+                                      prefix_shared=sum(len(users[k]) - 1 for k in tokens), prefix_passes=0)
+        claim = _Claim(pool)
+        with claim:
+            # cached prefixes first, so that reserving the new ones cannot evict them
+            for key, slot in cached.items():
+                claim.pin(slot, len(users[key]))
+            slot_of = dict(cached)
+            for key, ids in tokens.items():
+                slot_of[key] = claim.reserve(key, len(ids), len(users[key]))
+            buckets: dict[int, list[tuple[int, str]]] = {}
+            for key, ids in tokens.items():
+                buckets.setdefault(next(nb for nb in C.PREFIX_BUCKETS if nb >= max(len(ids), 1)), []).append(key)
+            for nb in sorted(buckets):
+                queue = buckets[nb]
+                for b in self.prefix_passes(nb, len(queue)):
+                    batch, queue = queue[:b], queue[b:]
+                    timing["prefix_ms"] += self._prefix_pass(b, nb, [(slot_of[k], k[0], tokens[k]) for k in batch])
                     timing["prefix_passes"] += 1
-                    written.update(reserved[k] for k in part)
-        except BaseException:
-            pool.unpin(pinned)
-            for slot in reserved.values():
-                if slot not in written:
-                    pool.release(slot)
-            raise
-        return slots, timing
+                    claim.written(slot_of[k] for k in batch)
+        return [slot_of[tuple(key)] for key in rows], timing     # type: ignore[index]
+
+
+class _Claim:
+    """The pins and reservations one ensure_prefixes call takes, undone together if the call fails: its pins are
+    returned and the reservations whose prefix pass never ran are released (their pages hold nothing)."""
+
+    def __init__(self, pool: Any) -> None:
+        self.pool = pool
+        self.pins: list[int] = []
+        self.unwritten: set[int] = set()
+
+    def pin(self, slot: int, times: int) -> None:
+        self.pool.pin([slot] * times)
+        self.pins += [slot] * times
+
+    def reserve(self, key: tuple[int, str], tokens: int, times: int) -> int:
+        slot = self.pool.reserve(key[0], key[1], tokens)
+        self.unwritten.add(slot)
+        self.pin(slot, times)
+        return slot
+
+    def written(self, slots: Any) -> None:
+        self.unwritten.difference_update(slots)
+
+    def __enter__(self) -> _Claim:
+        return self
+
+    def __exit__(self, kind: Any, error: Any, tb: Any) -> bool:
+        if kind is not None:
+            self.pool.unpin(self.pins)
+            for slot in self.unwritten:
+                self.pool.release(slot)
+        return False

@@ -6,8 +6,10 @@ prepare, predict_many, predict, add_adapter, remove_adapter), with the behaviour
 (runtime/python/src/jeff_runtime/local_engine.py:295-622): adapter generations so rows prepared before a reload are
 refused, runs of at most as many distinct prefixes as the pool surely holds, each run's prefixes made sure of and
 pinned, the token limit checked, the batched passes, and per-group results with the call's timing and per-row
-timing. The result and request types (EngineResult, Prepared) and the typed errors mirror jeff.engine and jeff.errors
-field for field, so the reference's scheduler and client read them unchanged.
+timing. The result and request types (EngineResult, Prepared) and the typed errors come from jeff_b200.errors: the
+reference's own jeff.engine and jeff.errors classes whenever its client package is importable, so the reference's
+Scheduler and Jeff client dispatch on this engine's results and errors unchanged (tests/test_reference_callers_cpu.py
+drives both over this engine), else stand-ins with the same names, fields and messages.
 
 What differs, and why: the reference's prepare() renders each row through the adapter's chat template and splits it
 with its tokenizer (prepare.prepare_rows, prepare.py:366-392). No tokenizer or prompt layout exists offline, so this
@@ -28,93 +30,19 @@ import math
 import threading
 import time
 from collections.abc import Callable, Sequence
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from pathlib import Path
 from typing import Any
 
 from jeff_b200 import constants as C
-from jeff_b200.prefix_pool import RESERVED_PAGES, EngineError
+from jeff_b200.errors import (BASE_ADAPTER, REFERENCE_TYPES, EngineError, EngineResult, InputTooLong, InvalidRequest,
+                              JeffError, NotInstalled, Prepared, TooManyLabels)
+from jeff_b200.prefix_pool import RESERVED_PAGES
 
-BASE_ADAPTER = "base"
 SUM_TOLERANCE = 1e-4
 TOO_LONG_MESSAGE = "no input was truncated"
-
-
-# ---------------------------------------------------------------- the reference's typed errors (jeff/errors.py)
-
-
-class JeffError(Exception):
-    """Base of the typed errors a group's result can carry instead of probabilities."""
-
-
-class NotInstalled(JeffError):
-    def __init__(self, function_id: str, why: str = "") -> None:
-        adapter = function_id.rsplit(".", 1)[0] if function_id.count(".") >= 3 else function_id
-        super().__init__(f"{function_id} is not installed{(': ' + why) if why else ''}. Install it with: jeff pull "
-                         f"{adapter}")
-        self.function_id = function_id
-
-
-class InvalidRequest(JeffError):
-    """A row the engine cannot read (missing fields)."""
-
-
-class InputTooLong(JeffError):
-    """A row whose prompt is longer than the engine's token limit."""
-
-
-class TooManyLabels(JeffError):
-    """A question with more options than the adapter was trained on."""
-
-
-# ---------------------------------------------------------------- request and result types (jeff/engine.py)
-
-
-@dataclass(frozen=True)
-class EngineResult:
-    """probabilities: one list per row over its options; timing for the group; input_tokens per row; row_timing
-    lists in row order (jeff/engine.py:21-34)."""
-    probabilities: list[list[float]]
-    timing: dict[str, Any] = field(default_factory=dict)
-    input_tokens: list[int] | None = None
-    row_timing: dict[str, list[Any]] | None = None
-
-
-@dataclass(frozen=True)
-class Prepared:
-    """A request's rows as prepare() left them (jeff/engine.py:37-80): rows, one item per row (its Row), the route
-    ("fast") and the adapter's load generation."""
-    rows: list[dict[str, Any]]
-    items: list[Any] | None = None
-    route: str | None = None
-    generation: Any = None
-
-    def __post_init__(self) -> None:
-        if self.items is not None and len(self.items) != len(self.rows):
-            raise EngineError(f"Prepared has {len(self.items)} items for {len(self.rows)} rows")
-
-    def part(self, start: int, stop: int) -> Prepared:
-        if start == 0 and stop == len(self.rows):
-            return self
-        return Prepared(self.rows[start:stop], None if self.items is None else self.items[start:stop], self.route,
-                        self.generation)
-
-    @staticmethod
-    def join(parts: Sequence[Prepared]) -> Prepared:
-        if len(parts) == 1:
-            return parts[0]
-        routes = {(part.route, part.generation) for part in parts}
-        if len(routes) != 1:
-            raise EngineError(f"Prepared.join was given parts of several routes or generations "
-                              f"{sorted(map(str, routes))}")
-        if all(part.items is None for part in parts):
-            items = None
-        elif any(part.items is None for part in parts):
-            raise EngineError("Prepared.join was given parts with items and parts without")
-        else:
-            items = [item for part in parts for item in part.items or []]
-        route, generation = routes.pop()
-        return Prepared([row for part in parts for row in part.rows], items, route, generation)
+ROW_TIMING = ("pass_rows", "bucket", "adapters_in_pass")
+CALL_COUNTERS = ("passes", "prefix_ms", "prefix_misses", "prefix_hits", "prefix_shared", "prefix_passes")
 
 
 # ---------------------------------------------------------------- the decision step (jeff/decision.py)
@@ -362,31 +290,25 @@ class B200Engine:
                                 "adapters_in_pass": pass_timing["adapters_in_pass"]}
 
     def _fast_many(self, groups: list[tuple[str, Prepared]]) -> list[EngineResult]:
+        """Every fast group of a predict_many call: the rows of all groups in order, cut into runs the pool holds
+        (_runs), each run's prefixes made sure of and its passes run; then each group gets its rows' slice of the
+        per-row lists, and the call-wide counters and wall time that every group of the call shares (the reference's
+        timing contract: local_engine.py:469-516)."""
         started = time.perf_counter()
         rows = [(self.fast.index(None if adapter_id == BASE_ADAPTER else adapter_id), item)
                 for adapter_id, prepared in groups for item in prepared.items or []]
-        values: list[list[float]] = []
-        tokens: list[int] = []
-        per_row: dict[str, list[Any]] = {"pass_rows": [], "bucket": [], "adapters_in_pass": []}
-        totals: dict[str, Any] = {name: 0 for name in ("passes", "prefix_ms", "prefix_misses", "prefix_hits",
-                                                       "prefix_shared", "prefix_passes")}
-        for run in self._runs(rows):
-            run_values, run_tokens, run_timing = self._fast_run(run)
-            values.extend(run_values)
-            tokens.extend(run_tokens)
-            for name in per_row:
-                per_row[name].extend(run_timing[name])
-            for name in totals:
-                totals[name] += run_timing[name]
-        shared = {"path": "fast", "model_ms": round((time.perf_counter() - started) * 1000, 3), **totals,
-                  **self.base_format}
-        results = []
-        offset = 0
-        for _, prepared in groups:
-            mine = slice(offset, offset + len(prepared.rows))
-            offset += len(prepared.rows)
-            results.append(EngineResult(
-                [list(map(float, row)) for row in values[mine]], dict(shared), [int(n) for n in tokens[mine]],
-                {**{name: per_row[name][mine] for name in per_row},
-                 "new_tokens": [len(item.new_ids) for item in prepared.items or []]}))
-        return results
+        done = [self._fast_run(run) for run in self._runs(rows)]
+        values = list(itertools.chain.from_iterable(d[0] for d in done))
+        tokens = list(itertools.chain.from_iterable(d[1] for d in done))
+        per_row = {name: list(itertools.chain.from_iterable(d[2][name] for d in done)) for name in ROW_TIMING}
+        shared: dict[str, Any] = {"path": "fast", "model_ms": round((time.perf_counter() - started) * 1000, 3)}
+        shared.update({name: sum(d[2][name] for d in done) for name in CALL_COUNTERS})
+        shared.update(self.base_format)
+        edges = list(itertools.accumulate((len(p.rows) for _, p in groups), initial=0))
+        out = []
+        for (_, prepared), lo, hi in zip(groups, edges, edges[1:], strict=False):
+            row_timing = {name: per_row[name][lo:hi] for name in ROW_TIMING}
+            row_timing["new_tokens"] = [len(item.new_ids) for item in prepared.items or []]
+            out.append(EngineResult([[float(p) for p in v] for v in values[lo:hi]], dict(shared),
+                                    [int(t) for t in tokens[lo:hi]], row_timing))
+        return out

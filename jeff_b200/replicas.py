@@ -94,9 +94,26 @@ def add_adapter_everywhere(fast, adapter, src: int = 0) -> int:
 
 def remove_adapter_everywhere(fast, name: str) -> None:
     """Remove an adapter on every rank (no data moves: the row is freed and its cached prefixes forgotten on each
-    rank); every rank must call this, in the same order."""
-    fast.remove_adapter(name)
-    barrier(_size())
+    rank); every rank must call this, in the same order. A rank whose own removal fails still joins the exchange of
+    outcomes, so no rank is left waiting in a collective; if any rank failed, every rank raises the same error."""
+    size = _size()
+    try:
+        fast.remove_adapter(name)
+        failure = None
+    except Exception as error:  # noqa: BLE001 - reported to every rank below
+        failure = f"{type(error).__name__}: {error}"
+    if size == 1:
+        if failure:
+            raise RuntimeError(f"Removing adapter {name} failed: {failure}")
+        return
+    import torch.distributed as dist
+
+    outcomes: list = [None] * size
+    dist.all_gather_object(outcomes, failure)
+    problems = "; ".join(f"rank {r}: {why}" for r, why in enumerate(outcomes) if why)
+    if problems:
+        raise RuntimeError(f"Removing adapter {name} failed on some ranks ({problems}); their adapter pools have "
+                           "drifted apart (add and remove the same adapters on every rank, in the same order)")
 
 
 def _size() -> int:

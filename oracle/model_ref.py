@@ -1,4 +1,5 @@
-"""TEST INFRASTRUCTURE ONLY (the checker, never the product): torch-CPU restatement of the batched decision pass.
+"""TEST INFRASTRUCTURE ONLY (the checker, never the product): torch restatement of the batched decision pass (CPU,
+or a GPU through to_device when a test runs it there as the checker).
 
 Each function restates one kernel of the reference's fast path with its bfloat16 rounding points, citing the
 reference (paths relative to runtime/python/src/jeff_runtime/engine/; "T5" is transformers'
@@ -57,17 +58,22 @@ def add_rms(x: torch.Tensor, d: torch.Tensor | None, w: torch.Tensor, exact: boo
 
 
 def product(x: torch.Tensor, W: torch.Tensor, lora: list[tuple[torch.Tensor, torch.Tensor] | None],
-            row_of_token: torch.Tensor, exact: bool = False) -> torch.Tensor:
-    """x (T, k) @ W^T plus each token's LoRA update: lora[row] = (A (R, k), B (out, R)) or None; row_of_token (T,)."""
-    y = x @ W.float().T
+            row_of_token: torch.Tensor, exact: bool = False, wide: bool = False) -> torch.Tensor:
+    """x (T, k) @ W^T plus each token's LoRA update: lora[row] = (A (R, k), B (out, R)) or None; row_of_token (T,).
+    wide: the sums in float64 before the same roundings (a second valid summation order, to measure how far two
+    float32-accumulating implementations with identical rounding points drift apart)."""
+    acc = torch.float64 if wide else torch.float32
+    xa = x.to(acc)
+    y = xa @ W.to(acc).T
     for row in torch.unique(row_of_token).tolist():
         pair = lora[row]
         if pair is None:
             continue
         a, b = pair
         sel = row_of_token == row
-        mid = x[sel] @ a.float().T
-        y[sel] = y[sel] + (mid if exact else bf(mid)) @ b.float().T
+        mid = (xa[sel] @ a.to(acc).T).float()
+        y[sel] = y[sel] + (mid if exact else bf(mid)).to(acc) @ b.to(acc).T
+    y = y.float()
     return y if exact else bf(y)
 
 
@@ -97,7 +103,7 @@ def gdn_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
     rule token by token: S <- S e^g; v' = beta (v - S^T k); S <- S + k v'^T; o = S^T q / sqrt(128). Returns o
     (B, N, 16, 128) float32 and the final state."""
     s = s0.float().clone()
-    out = torch.empty(v.shape, dtype=torch.float32)
+    out = torch.empty(v.shape, dtype=torch.float32, device=v.device)
     scale = DK ** -0.5
     for t in range(q.shape[1]):
         s = s * torch.exp(g[:, t])[..., None, None]
@@ -117,8 +123,8 @@ def gated_norm(o: torch.Tensor, z: torch.Tensor, w: torch.Tensor, exact: bool = 
     return r(y * (zz * torch.sigmoid(zz))).reshape(o.shape[0], -1)
 
 
-def inv_freq() -> torch.Tensor:
-    return 1.0 / (ROPE_THETA ** (torch.arange(0, ROT, 2, dtype=torch.float32) / ROT))
+def inv_freq(device: torch.device | str = "cpu") -> torch.Tensor:
+    return 1.0 / (ROPE_THETA ** (torch.arange(0, ROT, 2, dtype=torch.float32, device=device) / ROT))
 
 
 def attn_prep(pr: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor, pos0: int, exact: bool = False
@@ -132,8 +138,8 @@ def attn_prep(pr: torch.Tensor, q_w: torch.Tensor, k_w: torch.Tensor, pos0: int,
     queries, gate = qg[:, :, :HD], qg[:, :, HD:]
     keys = x[:, NQ * 2 * HD:NQ * 2 * HD + NKV * HD].view(n, NKV, HD)
     values = x[:, NQ * 2 * HD + NKV * HD:].view(n, NKV, HD)
-    positions = (pos0 + torch.arange(n)).float()
-    f = positions[:, None, None] * torch.cat([inv_freq(), inv_freq()])
+    positions = (pos0 + torch.arange(n, device=pr.device)).float()
+    f = positions[:, None, None] * torch.cat([inv_freq(pr.device), inv_freq(pr.device)])
     cos, sin = r(torch.cos(f)), r(torch.sin(f))
 
     def norm_rope(h: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
@@ -155,8 +161,8 @@ def attention(q: torch.Tensor, kp: torch.Tensor, vp: torch.Tensor, kn: torch.Ten
     keys = torch.cat([kp, kn]).float().repeat_interleave(NQ // NKV, 1)
     values = torch.cat([vp, vn]).float().repeat_interleave(NQ // NKV, 1)
     scores = torch.einsum("nhd,mhd->hnm", q.float(), keys) * HD ** -0.5
-    m = torch.arange(p + n)
-    allowed = (m[None, :] < p) | (m[None, :] - p <= torch.arange(n)[:, None])
+    m = torch.arange(p + n, device=q.device)
+    allowed = (m[None, :] < p) | (m[None, :] - p <= torch.arange(n, device=q.device)[:, None])
     scores = scores.masked_fill(~allowed, float("-inf"))
     if not round_weights:
         return torch.einsum("hnm,mhd->nhd", scores.softmax(-1), values)
@@ -180,7 +186,7 @@ def readout(h: torch.Tensor, W: torch.Tensor, count: int, temperature: float, ex
     logits = W.float() @ h.float()
     if not exact:
         logits = bf(logits)
-    logits = logits.masked_fill(torch.arange(W.shape[0]) >= count, -1e9)
+    logits = logits.masked_fill(torch.arange(W.shape[0], device=logits.device) >= count, -1e9)
     return (logits / temperature).softmax(-1)
 
 
@@ -195,11 +201,11 @@ class PrefixState:
     values: list[torch.Tensor] = field(default_factory=list)
 
     @staticmethod
-    def empty(gdn_layers: int, attn_layers: int) -> "PrefixState":
-        return PrefixState(0, [torch.zeros(3, QKV) for _ in range(gdn_layers)],
-                           [torch.zeros(NV, DK, DV) for _ in range(gdn_layers)],
-                           [torch.zeros(0, NKV, HD) for _ in range(attn_layers)],
-                           [torch.zeros(0, NKV, HD) for _ in range(attn_layers)])
+    def empty(gdn_layers: int, attn_layers: int, device: torch.device | str = "cpu") -> "PrefixState":
+        return PrefixState(0, [torch.zeros(3, QKV, device=device) for _ in range(gdn_layers)],
+                           [torch.zeros(NV, DK, DV, device=device) for _ in range(gdn_layers)],
+                           [torch.zeros(0, NKV, HD, device=device) for _ in range(attn_layers)],
+                           [torch.zeros(0, NKV, HD, device=device) for _ in range(attn_layers)])
 
 
 @dataclass
@@ -222,15 +228,16 @@ class PassOut:
 
 
 def run_pass(model, rows: list[RowIn], exact: bool = False, want_prefix: bool = False,
-             keep_all: bool = False) -> PassOut:
+             keep_all: bool = False, wide: bool = False) -> PassOut:
     """The forward of every row's tokens from its cached prefix (batched_path.py:242-276): rows may have different
     lengths. With want_prefix, also each row's state after its tokens (the prefix pass, batched_path.py:291-349),
-    starting from the row's given prefix state."""
+    starting from the row's given prefix state. wide: every product summed in float64 (see product)."""
     r = _r(exact)
     lengths = [len(row.ids) for row in rows]
     starts = [sum(lengths[:i]) for i in range(len(rows))]
-    row_of = torch.cat([torch.full((n,), i, dtype=torch.long) for i, n in enumerate(lengths)])
-    ids = torch.tensor([t for row in rows for t in row.ids], dtype=torch.long)
+    dev = model.embed.device
+    row_of = torch.cat([torch.full((n,), i, dtype=torch.long, device=dev) for i, n in enumerate(lengths)])
+    ids = torch.tensor([t for row in rows for t in row.ids], dtype=torch.long, device=dev)
     x = model.embed[ids].float()
     d: torch.Tensor | None = None
     gi = ai = 0
@@ -243,7 +250,7 @@ def run_pass(model, rows: list[RowIn], exact: bool = False, want_prefix: bool = 
 
     for li, layer in enumerate(model.layers):
         x, h = add_rms(x, d, layer.norm_in, exact)
-        pr = product(h, layer.groups["proj"].W, lora_of(li, "proj"), row_of, exact)
+        pr = product(h, layer.groups["proj"].W, lora_of(li, "proj"), row_of, exact, wide)
         ys = []
         if layer.kind == "linear_attention":
             by_len: dict[int, list[int]] = {}
@@ -278,16 +285,16 @@ def run_pass(model, rows: list[RowIn], exact: bool = False, want_prefix: bool = 
                     outs[i].values.append(torch.cat([vp.float(), vn.float()]))
             ai += 1
         y = torch.cat(ys, 0)
-        d = product(y, layer.groups["out"].W, lora_of(li, "out"), row_of, exact)
+        d = product(y, layer.groups["out"].W, lora_of(li, "out"), row_of, exact, wide)
         x, h = add_rms(x, d, layer.norm_post, exact)
-        gu = product(h, layer.groups["mlp_in"].W, lora_of(li, "mlp_in"), row_of, exact)
-        d = product(silu_mul(gu, exact), layer.groups["mlp_down"].W, lora_of(li, "mlp_down"), row_of, exact)
+        gu = product(h, layer.groups["mlp_in"].W, lora_of(li, "mlp_in"), row_of, exact, wide)
+        d = product(silu_mul(gu, exact), layer.groups["mlp_down"].W, lora_of(li, "mlp_down"), row_of, exact, wide)
         resid = x + d if exact else bf(x + d)
         layer_last.append([resid[starts[i] + lengths[i] - 1].clone() for i in range(len(rows))])
         if keep_all:
             layer_all.append(resid.clone())
     assert d is not None
-    last = torch.tensor([starts[i] + lengths[i] - 1 for i in range(len(rows))])
+    last = torch.tensor([starts[i] + lengths[i] - 1 for i in range(len(rows))], device=dev)
     xl = x[last] + d[last]
     if not exact:
         xl = bf(xl)
@@ -304,6 +311,24 @@ def decision(probs: torch.Tensor, count: int, threshold: float) -> tuple[int, fl
     best = int(torch.argmax(p))
     conf = float(p[best])
     return best, conf, conf < threshold
+
+
+def to_device(obj, device: torch.device | str):
+    """A copy of a weights object (dataclasses, dicts, lists and tuples of tensors: a model, an adapter, a prefix
+    state) with every tensor moved to `device`, so the oracle can run as a checker on a GPU box; the arithmetic is
+    the same float32 restatement wherever it runs."""
+    import dataclasses
+
+    if isinstance(obj, torch.Tensor):
+        return obj.to(device)
+    if dataclasses.is_dataclass(obj) and not isinstance(obj, type):
+        return dataclasses.replace(obj, **{f.name: to_device(getattr(obj, f.name), device)
+                                          for f in dataclasses.fields(obj) if f.init})
+    if isinstance(obj, dict):
+        return {k: to_device(v, device) for k, v in obj.items()}
+    if isinstance(obj, (list, tuple)):
+        return type(obj)(to_device(v, device) for v in obj)
+    return obj
 
 
 def rel_error(a: torch.Tensor, b: torch.Tensor) -> float:

@@ -209,6 +209,12 @@ def _adapter_rank_main(rank: int, port: int, errors) -> None:
         except RuntimeError as error:
             assert "different rows" in str(error)
         assert "d" not in pools.adapter_index
+        # a removal that fails on one rank (rank 0 never loaded "local") raises on both, and neither is left waiting
+        try:
+            replicas.remove_adapter_everywhere(pools, "local")
+            raise AssertionError("a removal that failed on rank 0 was not reported")
+        except RuntimeError as error:
+            assert "rank 0" in str(error) and "Removing adapter local" in str(error)
         replicas.barrier(2)
         dist.destroy_process_group()
     except BaseException:
