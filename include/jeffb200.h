@@ -160,6 +160,20 @@ int jb_gdn_scan_recurrent(const uint16_t* q, const uint16_t* k, const uint16_t* 
                           const int32_t* tables, int table_stride, int first_head, int heads_per_page,
                           const int32_t* last, const int32_t* out_tables, int out_table_stride, void* stream);
 
+/* A Gated DeltaNet layer's mixer in one launch: jb_gdn_prep_rows, jb_gdn_scan and jb_gated_norm fused (one CTA per
+ * (row, head); q, k, v, g, beta and o stay on chip): y (t, ldy >= 2048) bf16, column block [128 h, 128 h + 128) for
+ * head h, from pr (t, ldpr) = [q | k | v | z | b | a], bit-identical to the three calls in sequence. The state of
+ * flat head first_head + h and the layer's conv tail (tables[r][conv_entry], slot conv_slot) are read in place;
+ * last (nullable, the decision pass): outputs past last[r] are those of o = 0; real and out_tables (nullable, the
+ * prefix pass): tokens from real[r] on leave the state unchanged, each row's final state and last three real conv
+ * inputs go to its own pages. Replaces the Gated DeltaNet part of batched_path.body (batched_path.py:269-289:
+ * gdn_prep_rows, fla's chunk_gated_delta_rule, the gated norm of fast_path.py:103-120). */
+int jb_gdn_layer(const uint16_t* pr, int ldpr, int t, int n, void* pool, int64_t page_bytes, const int32_t* tables,
+                 int table_stride, int first_head, int heads_per_page, int conv_entry, int conv_slot,
+                 const float* conv_w, const float* a_neg, const float* dt_bias, const uint16_t* gnorm_w, uint16_t* y,
+                 int ldy, const int32_t* last, const int32_t* real, const int32_t* out_tables, int out_table_stride,
+                 void* stream);
+
 /* ---------------------------------------------------------------- attention (S3) */
 
 /* Attention input side: per token q/k per-head RMSNorm * w1 -> bf16, RoPE on the first 64 dims at position

@@ -16,7 +16,9 @@ cfg2: the projection sweep over one decoder layer (q 1024->2048, k and v 1024->5
 cfg3: one Gated DeltaNet prefill layer: 64 rows x 256 new tokens, each from a pooled fp32 state ~ N(0, 0.1). The
   prep kernel (conv width 4 + SiLU + L2 norms + gates from the projection output) reads 201 MB of q/k/v inputs,
   1 MB of gates and 2.4 MB of convolution tails and writes 201 MB of q/k/v and 1.5 MB of g/beta; the chunked scan
-  reads q, k, v (201 MB), g and beta (1.5 MB) and the states (67 MB) and writes o (67 MB): 337 MB.
+  reads q, k, v (201 MB), g and beta (1.5 MB) and the states (67 MB) and writes o (67 MB): 337 MB. The fused mixer
+  (jb_gdn_layer: prep, scan and gated norm in one launch) reads the projection output (270 MB: q | k | v | z | b | a),
+  the tails and the states and writes y (67 MB): 406 MB, with q, k, v and o never in HBM.
 
 One JSON line per kernel: milliseconds per call, GB/s of algorithmic bytes, and the fraction of the measured HBM copy
 bandwidth (MEASURED_PEAKS.json beside the repository root when present); for cfg2 also TFLOP/s and the fraction of
@@ -182,12 +184,25 @@ def cfg3(reps: int) -> list[dict]:
     prep_ms = timed(lambda: kernels.gdn_prep_rows(pr, pool, tables, 0, conv_w, a_neg, dt_bias, n, outs=outs), reps)
     q, k, v, gg, beta = outs
     scan_ms = timed(lambda: kernels.gdn_scan(q, k, v, gg, beta, pool, tables, 0, out=o), reps)
+    gnorm = torch.ones(C.DV, dtype=torch.bfloat16, device="cuda")
+    y = torch.empty(t, C.NV * C.DV, dtype=torch.bfloat16, device="cuda")
+    norm_ms = timed(lambda: kernels.gated_norm(o.view(t, C.NV, C.DV), pr, gnorm, out=y), reps)
+    layer_ms = timed(lambda: kernels.gdn_layer(pr, pool, tables, 0, conv_w, a_neg, dt_bias, gnorm, n, out=y), reps)
     qkv = t * C.QKV_DIM * 2
-    prep_bytes = qkv + t * 2 * C.NV * 2 + rows * 3 * C.QKV_DIM * 2 + 4 * C.QKV_DIM * 4 + qkv + t * C.NV * (4 + 2)
-    scan_bytes = qkv + t * C.NV * (4 + 2) + rows * C.NV * C.DK * C.DV * 4 + t * C.NV * C.DV * 2
-    return [{"kernel": "gdn prep_kernel", "config": "cfg3 64 rows x 256 tokens", "ms": prep_ms, "bytes": prep_bytes},
-            {"kernel": "gdn chunk_kernel (scan from pooled state)", "config": "cfg3 64 rows x 256 tokens",
-             "ms": scan_ms, "bytes": scan_bytes}]
+    tails = rows * 3 * C.QKV_DIM * 2 + 4 * C.QKV_DIM * 4
+    states = rows * C.NV * C.DK * C.DV * 4
+    prep_bytes = qkv + t * 2 * C.NV * 2 + tails + qkv + t * C.NV * (4 + 2)
+    scan_bytes = qkv + t * C.NV * (4 + 2) + states + t * C.NV * C.DV * 2
+    norm_bytes = 3 * t * C.NV * C.DV * 2
+    # the fused mixer reads the projection output's q | k | v | z | b | a, the tails, taps and states, writes y
+    layer_bytes = t * C.GDN_PROJ * 2 + tails + states + t * C.NV * C.DV * 2
+    config = "cfg3 64 rows x 256 tokens"
+    return [{"kernel": "gdn prep_kernel", "config": config, "ms": prep_ms, "bytes": prep_bytes},
+            {"kernel": "gdn chunk_kernel (scan from pooled state)", "config": config, "ms": scan_ms,
+             "bytes": scan_bytes},
+            {"kernel": "gated_norm_kernel", "config": config, "ms": norm_ms, "bytes": norm_bytes},
+            {"kernel": "gdn layer_kernel (prep + scan + gated norm fused)", "config": config, "ms": layer_ms,
+             "bytes": layer_bytes, "unfused_ms": prep_ms + scan_ms + norm_ms}]
 
 
 def main() -> None:

@@ -215,6 +215,38 @@ def gdn_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
     return o
 
 
+def gdn_layer(pr: torch.Tensor, pool, tables: torch.Tensor, gdn_layer: int, conv_w: torch.Tensor,
+              a_neg: torch.Tensor, dt_bias: torch.Tensor, gnorm_w: torch.Tensor, n: int,
+              last: torch.Tensor | None = None, real: torch.Tensor | None = None,
+              out_tables: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """A Gated DeltaNet layer's mixer in one launch (gdn_prep_rows, the chunked rule and gated_norm fused): y
+    (t, 2048) bf16 from the in_proj output pr (t, 8224), each row resuming from its pooled state and conv tail.
+    last: the decision pass's last real token per row; real + out_tables: the prefix pass."""
+    t = pr.shape[0]
+    _pass_rows(t, n)
+    shapes = pool.shapes
+    if tables.dim() != 2 or tables.shape[0] < t // n or tables.shape[1] < shapes.fixed_pages or \
+            tables.dtype != torch.int32:
+        raise ValueError(f"tables: expected int32 (rows >= {t // n}, width >= {shapes.fixed_pages}), got "
+                         f"{tuple(tables.shape)} {tables.dtype}")
+    if conv_w.shape != (4, C.QKV_DIM) or conv_w.dtype != torch.float32 or not conv_w.is_contiguous():
+        raise ValueError(f"gdn_layer: conv_w must be a contiguous float32 (4, {C.QKV_DIM}) tensor, got "
+                         f"{tuple(conv_w.shape)}, {conv_w.dtype}")
+    if gnorm_w.shape != (C.DV,) or gnorm_w.dtype != DT or not gnorm_w.is_contiguous():
+        raise ValueError(f"gdn_layer: gnorm_w must be a contiguous bf16 ({C.DV},) vector")
+    if pr.stride(1) != 1 or pr.shape[1] < C.GDN_PROJ:
+        raise ValueError(f"gdn_layer: pr must be row-major with at least {C.GDN_PROJ} columns")
+    y = out if out is not None else torch.empty(t, C.NV * C.DV, dtype=DT, device=pr.device)
+    if y.stride(1) != 1 or y.shape[1] < C.NV * C.DV:
+        raise ValueError("gdn_layer: out must be row-major with at least 2048 columns")
+    per = shapes.layers_per_conv_page
+    _lib.call("jb_gdn_layer", ptr(pr), pr.stride(0), t, n, ptr(pool.data), shapes.page_bytes, ptr(tables),
+              tables.stride(0), shapes.state[0] * gdn_layer, shapes.heads_per_page, shapes.state_pages + gdn_layer // per,
+              gdn_layer % per, ptr(conv_w), ptr(a_neg), ptr(dt_bias), ptr(gnorm_w), ptr(y), y.stride(0), ptr(last),
+              ptr(real), ptr(out_tables), 0 if out_tables is None else out_tables.stride(0), stream_ptr())
+    return y
+
+
 # ---------------------------------------------------------------- attention
 
 
