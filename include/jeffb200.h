@@ -26,6 +26,8 @@ extern "C" {
 #define JB_ETIMEOUT (-3) /* a device-side bounded wait gave up (see jb_device_status) */
 #define JB_DEV_TIMEOUT 0x10000 /* device status word: a bounded wait gave up; low bits say where */
 #define JB_PRODUCT_SWIGLU 1    /* product flag: columns are gate|up blocks of 64; y = bf16(bf16(silu(g)) u) */
+#define JB_PRODUCT_TMEM_A 2    /* product flag: the tensor-memory form (weights dequantised straight into tensor
+                                  memory as the MMA's A operand) where it applies; the same bits, measured slower */
 #define JB_PRODUCT_STATIC_MID_MAX 1048576 /* m * rank limit of jb_int4_lora_product_static (2 MiB of bf16) */
 
 /* ABI version of this header (bumped on any signature change): 2. */
@@ -36,11 +38,6 @@ const char* jb_last_error(void);
  * Synchronises `stream`. Not for use inside graph capture. */
 int jb_device_status(int* status, int reset, void* stream);
 
-/* The product kernel's stage trace: out (16 x 256 uint64) receives clock64() stamps of CTA 0's hand-offs for its
- * first 256 K blocks in the last launch (event rows as described in csrc/w4a16_gemm.cu). Only a library built with
- * -DJB_TRACE (libjeffb200_trace.so) records them; the product library returns JB_EINVAL. A measurement aid with no
- * reference counterpart. */
-int jb_stage_trace_read(uint64_t* out);
 
 /* ---------------------------------------------------------------- int4 W4A16 + multi-LoRA products (S1) */
 

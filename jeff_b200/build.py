@@ -4,8 +4,9 @@
 
 One translation unit (csrc/lib.cu includes the kernel files), the CUDA runtime linked statically, so the library
 loads anywhere the driver exists (and, without a GPU, still loads and exports its symbols). --trace builds
-libjeffb200_trace.so beside it, with the product kernel's stage trace compiled in (-DJB_TRACE; jeff_b200.stage_trace
-reads it); the library the package loads is always the one without."""
+libjeffb200_trace.so beside it, with the shared-memory product kernel's stage trace compiled in (-DJB_TRACE, read out
+by its extra entry jb_stage_trace_read, a measurement aid outside the product header); the library the package loads
+is always the one without. Without --force an up-to-date library (newer than every source) is kept."""
 
 from __future__ import annotations
 

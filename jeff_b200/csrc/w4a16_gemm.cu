@@ -316,7 +316,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int kb = 0; kb < nkt; ++kb, ++kg) {
           const int s = kg % STAGES;
           const uint32_t ph = (kg / STAGES) & 1;
-          ok = mbar_wait(&full[s], ph, abort_flag, p.err, 3) && mbar_wait(&deq[s], ph, abort_flag, p.err, 4);
+          // one wait: the dequantisers arrive on deq[s] only after each of them saw full[s] complete (the stage's
+          // TMA bytes landed), so deq[s] covers both
+          ok = mbar_wait(&deq[s], ph, abort_flag, p.err, 4);
           if (!ok) break;
           JB_STAGE(4, kg);
           tc_fence_after();
@@ -759,19 +761,17 @@ template <bool ZERO>
 int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ts, const CUtensorMap& tz,
            const CUtensorMap& tm, const CUtensorMap& tl, const Params& p, cudaStream_t stream) {
   auto kernel = w4a16_lora_kernel<ZERO>;
-  static bool configured[64] = {};
-  static int sms[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !configured[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout::ALLOC);
-    if (e != cudaSuccess) return status_of(e, "w4a16: cudaFuncSetAttribute");
-    e = cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return status_of(e, "w4a16: SM count");
-    configured[dev] = true;
-  }
+  // queried on every call (well under a microsecond each): the attribute and the SM count belong to the current
+  // device, and no per-device cache is shared between host threads
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return status_of(e, "w4a16: cudaGetDevice");
+  e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout::ALLOC);
+  if (e != cudaSuccess) return status_of(e, "w4a16: cudaFuncSetAttribute");
+  e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return status_of(e, "w4a16: SM count");
   const int tiles = p.m_tiles * p.n_tiles;
-  const int grid = tiles < sms[dev] ? tiles : sms[dev];
+  const int grid = tiles < sms ? tiles : sms;
   kernel<<<grid, THREADS, Layout::ALLOC, stream>>>(tx, tw, ts, tz, tm, tl, p);
   return check_launch("w4a16_lora_kernel");
 }
@@ -789,6 +789,8 @@ __global__ void int4_repack_kernel(const int32_t* __restrict__ in, int32_t* __re
 
 }  // namespace w4
 }  // namespace jb
+
+#include "w4a16_tmem.cu"
 
 using namespace jb;
 
@@ -878,6 +880,12 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
                  w4::Layout::MAX_ROWS);
     }
   }
+  // JB_PRODUCT_TMEM_A: the tensor-memory form (w4a16_tmem.cu), for calls whose LoRA rows are whole 128-token halves
+  // (or one row for the whole pass); the same bits. Measured on a B200 at the Gated DeltaNet in_proj shape it takes
+  // 245 us against 162 us for the shared-memory form below, so it is not the default.
+  if ((flags & JB_PRODUCT_TMEM_A) && (!lora || row_len % w4t::HT == 0 || m <= row_len))
+    return w4t::launch(x, m, k, words, scales, zeros, group, columns, out, mid, lora_b, rank, pool_rows, adapters,
+                       row_len, y, ldy, swiglu, (cudaStream_t)stream);
   CUtensorMap tx, tw, ts, tz, tm, tl;
   int st;
   constexpr int BN = w4::BN;
@@ -928,17 +936,16 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
   return w4::launch<false>(tx, tw, ts, tz, tm, tl, p, (cudaStream_t)stream);
 }
 
+#ifdef JB_TRACE
+// Measurement builds only (python -m jeff_b200.build --trace, libjeffb200_trace.so): copies the shared-memory
+// product kernel's stage trace, 16 x 256 clock64() stamps of CTA 0's hand-offs in its last launch, to `out`. Not
+// part of the product library or its header.
 extern "C" int jb_stage_trace_read(uint64_t* out) {
   JB_REQUIRE(out, "jb_stage_trace_read: null pointer");
-#ifdef JB_TRACE
   return status_of(cudaMemcpyFromSymbol(out, w4::g_stage_trace, sizeof(w4::g_stage_trace)),
                    "jb_stage_trace_read: copy");
-#else
-  set_error("jb_stage_trace_read: this library was built without the stage trace (python -m jeff_b200.build "
-            "--trace builds libjeffb200_trace.so with it)");
-  return JB_EINVAL;
-#endif
 }
+#endif
 
 extern "C" int jb_int4_repack(const int32_t* words, int32_t* out, int k, int columns, void* stream) {
   JB_REQUIRE(words && out, "jb_int4_repack: null pointer");

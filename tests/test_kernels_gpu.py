@@ -195,6 +195,50 @@ def test_int4_lora_product_swiglu_epilogue(fmt: str) -> None:
     torch.testing.assert_close(got, want, rtol=4 * BF16_STEP, atol=5e-4)
 
 
+@pytest.mark.parametrize("fmt", ["g128z", "g64"])
+@pytest.mark.parametrize(("m", "k", "out", "rank", "row_len", "swiglu"), [
+    (64, 1024, 3584, 16, 64, False),        # configuration 1: one row for the whole pass
+    (256, 1024, 8224, 48, 128, False),      # the Gated DeltaNet projection (columns not a multiple of 128)
+    (384, 2048, 1024, 16, 128, False),      # out_proj
+    (200, 3584, 1024, 16, 256, False),      # down_proj, K = 3584, m past the last full tile
+    (512, 1024, 7168, 32, 128, True),       # gate|up with the SwiGLU epilogue
+    (1000, 1024, 4608, 0, 128, False),      # no LoRA, ragged m
+])
+def test_tensor_memory_product_gives_the_bits_of_the_shared_memory_form(fmt: str, m: int, k: int, out: int,
+                                                                         rank: int, row_len: int,
+                                                                         swiglu: bool) -> None:
+    """The tensor-memory form (JB_PRODUCT_TMEM_A: weights dequantised into tensor memory as the MMA's A operand,
+    tokens as N) against the shared-memory form on the same inputs: every bit the same (each output is the same fp32
+    sum in the same K order, rounded once), with and without LoRA and SwiGLU, both int4 formats, ragged m and
+    columns. The shared-memory form is itself held to the float64 error bound above."""
+    from jeff_b200.fast_path import swiglu_order
+
+    g = torch.Generator().manual_seed(m + k + out + rank)
+    w = torch.randn(out, k, generator=g) * 0.02
+    packed, _ = prod_int4.quantize_pack(w, fmt)
+    words, scales, zeros = packed.words, packed.scales, packed.zeros
+    if swiglu:
+        order = swiglu_order(out // 2)
+        words, scales = words[:, order], scales[:, order]
+        zeros = None if zeros is None else zeros[:, order]
+    pool_rows = 4
+    lora_a = lora_b = adapters = None
+    if rank:
+        lora_a = (torch.randn(pool_rows, rank, k, generator=g) * 0.02).to(torch.bfloat16).cuda()
+        lora_b = torch.zeros(pool_rows, packed.columns, rank, dtype=torch.bfloat16)
+        lora_b[:, :out] = (torch.randn(pool_rows, out, rank, generator=g) * 0.05).to(torch.bfloat16)
+        lora_b = lora_b.cuda()
+        adapters = torch.randint(-1, pool_rows + 1, (-(-m // row_len),), generator=g, dtype=torch.int32).cuda()
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16).cuda()
+    args = (x, kernels.int4_repack(words.contiguous().cuda()), scales.contiguous().cuda(),
+            None if zeros is None else zeros.contiguous().cuda(), packed.group, out, lora_a, lora_b, adapters,
+            row_len)
+    tm = kernels.int4_product(*args, swiglu=swiglu, tmem_a=True)
+    sm = kernels.int4_product(*args, swiglu=swiglu)
+    assert torch.equal(tm.view(torch.int16), sm.view(torch.int16)), \
+        f"{int((tm != sm).sum())} of {tm.numel()} outputs differ, max {float((tm.float() - sm.float()).abs().max())}"
+
+
 @pytest.mark.parametrize(("m", "k", "rank", "row_len"), [
     (256, 1024, 48, 64),      # staged kernel (32-row blocks of one adapter)
     (512, 3584, 16, 128),     # staged, K = 3584
