@@ -186,6 +186,16 @@ int jb_attn_prep_rows(const uint16_t* pr, int ldpr, int t, int n, const float* q
 int jb_paged_attention(const uint16_t* q, const void* pool, int64_t page_bytes, const int32_t* tables,
                        int table_stride, int kv_entry, int attn_layer, int attn_layers, const int32_t* pos,
                        const uint16_t* kn, const uint16_t* vn, uint16_t* out, int b, int n, void* stream);
+/* Paged prefix-KV attention with the output gate, on tcgen05: y (b n, ldy >= 2048) bf16 = bf16(bf16(O) *
+ * bf16(sigmoid(gate))), O the softmax(q k^T / 16) v of each query over its row's prefix keys (pool pages
+ * tables[r][kv_entry + j / 32] of the pool's pool_pages pages, attention layer attn_layer) and its own new keys
+ * causally, the gate the second half of each head's q_proj output in pr (t, ldpr). S and O in tensor memory, P
+ * rounded to bf16 before P V. n a multiple of 32. Replaces batched_kernels.paged_attention (batched_kernels.py:
+ * 370-486) followed by fast_path.gate_mul (fast_path.py:123-138). */
+int jb_paged_attention_gated(const uint16_t* q, const void* pool, int64_t pool_pages, int64_t page_bytes,
+                             const int32_t* tables, int table_stride, int kv_entry, int attn_layer, int attn_layers,
+                             const int32_t* pos, const uint16_t* kn, const uint16_t* vn, const uint16_t* pr, int ldpr,
+                             uint16_t* y, int ldy, int b, int n, void* stream);
 /* The prefix pass's page scatter: each row's new keys/values (tokens below ceil(real[r] / 32) * 32) into its
  * pages out_tables[r][kv_entry + j / 32] of attention layer attn_layer. Replaces pool.kv.index_copy_
  * (batched_path.py:345-349). */

@@ -92,6 +92,9 @@ class BatchedPath:
         # instructions then run inside the scan's one 8-warp CTA per SM, which issues on 30% of cycles (latency
         # bound), where the separate prep kernel runs them at full occupancy. So the pass keeps the three launches.
         self.fused_gdn = False
+        # attention: the tcgen05 kernel with the output gate fused (jb_paged_attention_gated); False runs the mma.sync
+        # kernel and jb_gate_mul (the same result within the attention tolerance, tested)
+        self.tc_attention = True
         self.tokenize = tokenize
         self.max_tokens = max_tokens
         dev = fast.device
@@ -187,8 +190,11 @@ class BatchedPath:
                     kernels.kv_scatter(kn, vn, n, real, pool, out_tables, ai)
                     if li == len(f.layers) - 1:
                         return None   # the last layer: only its keys and values are kept
-                ao = kernels.paged_attention(aq, pool, attn_tables, ai, pos, kn, vn, n, out=ws.ao[:t])
-                y = kernels.gate_mul(ao, pr, out=ws.y[:t])
+                if self.tc_attention:
+                    y = kernels.paged_attention_gated(aq, pool, attn_tables, ai, pos, kn, vn, n, pr, out=ws.y[:t])
+                else:
+                    ao = kernels.paged_attention(aq, pool, attn_tables, ai, pos, kn, vn, n, out=ws.ao[:t])
+                    y = kernels.gate_mul(ao, pr, out=ws.y[:t])
                 ai += 1
             d = layer["out"](y, adapters, n, ws.mid, ws.d[:t])
             _, h = kernels.add_rms(x, d, layer["norm_post"], xo=x, h=ws.h[:t])

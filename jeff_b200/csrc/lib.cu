@@ -116,6 +116,7 @@ int make_tmap_planes(CUtensorMap* map, const void* base, uint64_t rows, uint32_t
 #include "gdn.cu"
 #include "gdn_chunk.cu"
 #include "attention.cu"
+#include "attention_tc.cu"
 
 extern "C" int jb_abi_version(void) { return 2; }
 

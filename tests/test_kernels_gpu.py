@@ -680,6 +680,77 @@ def test_attn_prep_rows_match_the_oracle(pool_fixture, b: int, n: int) -> None:
 ATTN_RTOL, ATTN_ATOL = 2.0 ** -6, 2.0 ** -8
 
 
+def attention_inputs(t: int, seed: int):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(t, C.NQ, C.HD, generator=g).to(torch.bfloat16)
+    kn = torch.randn(t, C.NKV, C.HD, generator=g).to(torch.bfloat16)
+    vn = torch.randn(t, C.NKV, C.HD, generator=g).to(torch.bfloat16)
+    pr = torch.randn(t, C.ATTN_PROJ, generator=g).to(torch.bfloat16)   # the gate halves of q_proj are read
+    return q, kn, vn, pr
+
+
+def gated_oracle(q, kp, vp, kn, vn, pr_rows):
+    """bf16(bf16(attention) * bf16(sigmoid(gate))) per token (the reference's paged_attention then gate_mul)."""
+    o = model_ref.bf(model_ref.attention(q, kp, vp, kn, vn))
+    gate = pr_rows[:, :C.NQ * 2 * C.HD].float().view(-1, C.NQ, 2 * C.HD)[:, :, C.HD:]
+    return model_ref.gate_mul(o, gate)
+
+
+@pytest.mark.parametrize("b", BATCHES)
+@pytest.mark.parametrize("n", [32, 64, 128])
+def test_gated_attention_on_tensor_memory_matches_the_oracle(pool_fixture, b: int, n: int) -> None:
+    """The tcgen05 kernel (S and O in tensor memory, K / V pages by TMA, the gate fused): prefix keys read in place
+    from pages that hold NaN past each prefix's end (those V rows must be zeroed, not multiplied by zero), prefixes of
+    0 to 1,000 tokens (partial pages, a partial last tile of 64 keys), the new keys causally, attention layers 0 and 5.
+    Against the oracle's attention and gate multiply within ATTN_RTOL (plus one bf16 step for the second rounding) and
+    ATTN_ATOL; and against the mma.sync kernel + jb_gate_mul within twice that (each is within it of the exact
+    result)."""
+    pool, slots, states = pool_fixture
+    ss = pass_slots(slots, b, seed=b * 13 + n)
+    tables, pos = tables_for(pool, ss)
+    q, kn, vn, pr = attention_inputs(b * n, seed=b * 3 + n)
+    for layer in (0, 5):
+        got = kernels.paged_attention_gated(q.cuda(), pool, tables, layer, pos, kn.cuda(), vn.cuda(), n,
+                                            pr.cuda()).cpu()
+        assert not got.isnan().any(), "the kernel let a NaN past a prefix's last token into the sums"
+        old = kernels.gate_mul(kernels.paged_attention(q.cuda(), pool, tables, layer, pos, kn.cuda(), vn.cuda(), n),
+                               pr.cuda()).cpu()
+        # two implementations each within the tolerance of the exact result: within twice it of each other
+        torch.testing.assert_close(got.float(), old.float(), rtol=2 * (ATTN_RTOL + BF16_STEP), atol=2 * ATTN_ATOL)
+        for r in range(b):
+            kv = states[ss[r]][2][layer]
+            sl = slice(r * n, (r + 1) * n)
+            want = gated_oracle(q[sl], kv[0], kv[1], kn[sl], vn[sl], pr[sl])
+            torch.testing.assert_close(got[sl].float(), want, rtol=ATTN_RTOL + BF16_STEP, atol=ATTN_ATOL)
+
+
+def test_gated_attention_at_configuration_4() -> None:
+    """Configuration 4's attention: 64 rows of 128 new tokens, each over its own 512-token prefix (16 pages of a pool
+    written with random keys and values), both attention layers that bracket the layout (0 and 5); against the oracle
+    run on this GPU as the checker, within ATTN_RTOL (+ one bf16 step) and ATTN_ATOL."""
+    b, n, plen = 64, 128, 512
+    pool = PrefixPool(2 + b * (50 + plen // 32) + 4, "cuda")
+    sh = pool.shapes
+    g = torch.Generator().manual_seed(4)
+    slots = [pool.reserve(1, f"cfg4 attention {r}", plen) for r in range(b)]
+    kvs = []
+    for slot in slots:
+        kv = torch.randn(sh.attn_layers, 2, plen, *sh.kv, generator=g).to(torch.bfloat16)
+        pool.write(slot, torch.zeros(sh.gdn_layers, *sh.conv), torch.zeros(sh.gdn_layers, *sh.state), kv.cuda())
+        kvs.append(kv.cuda())
+    tables, pos = tables_for(pool, slots)
+    q, kn, vn, pr = (x.cuda() for x in attention_inputs(b * n, seed=44))
+    for layer in (0, 5):
+        got = kernels.paged_attention_gated(q, pool, tables, layer, pos, kn, vn, n, pr)
+        worst = 0.0
+        for r in range(b):
+            sl = slice(r * n, (r + 1) * n)
+            want = gated_oracle(q[sl], kvs[r][layer, 0], kvs[r][layer, 1], kn[sl], vn[sl], pr[sl])
+            torch.testing.assert_close(got[sl].float(), want, rtol=ATTN_RTOL + BF16_STEP, atol=ATTN_ATOL)
+            worst = max(worst, float((got[sl].float() - want).abs().max()))
+        print(f"configuration 4 attention layer {layer}: max |y - y_oracle| {worst:.2e}")
+
+
 @pytest.mark.parametrize("b", BATCHES)
 @pytest.mark.parametrize("n", [32, 64])
 def test_paged_attention_matches_the_oracle(pool_fixture, b: int, n: int) -> None:
