@@ -6,7 +6,7 @@
 // Keys are walked in tiles of 64: the prefix's pool pages two at a time (the page of token j is tables[r][kv_entry +
 // j / 32]), then the row's own new keys up to the block's last token. Per tile:
 //   S = Q K^T      tcgen05.mma M 128, N 64, K 256 (16 steps) into one of two S buffers in tensor memory;
-//   softmax        4 warps, thread = query row (its tensor-memory lane): masks (prefix keys past the prefix length,
+//   softmax        8 warps, thread = half a query row (its tensor-memory lane): masks (prefix keys past the prefix length,
 //                  new keys after the row's own token), the running max in log2 units, P = exp2(s - m) rounded to
 //                  bf16 (the reference's rounding point, batched_kernels.py:405-427) written to shared memory in the
 //                  MMA's 128B-swizzled layout, the row sum from the unrounded values; V rows of keys past the prefix
@@ -17,7 +17,8 @@
 // the previous value product and rescales O in tensor memory. The epilogue divides by the row sum, rounds O to bf16,
 // multiplies by bf16(sigmoid(gate)) (the gate half of the row's q_proj output) and rounds again: the reference's
 // gate_mul (fast_path.py:123-138), written straight into the o_proj input y (t, 2048).
-// Warps: 0 TMA producer, 1 tensor-memory allocation + MMA issue (one thread), 2-5 softmax and epilogue. Every wait
+// Warps: 0 TMA producer, 1 tensor-memory allocation + MMA issue (one thread), 2-9 softmax and epilogue (two warps per
+// row: each takes half of a tile's scores and half of O's columns; the halves' maxima meet in shared memory). Every wait
 // is bounded (2 s of %globaltimer): a lost arrival ends the kernel with a device status instead of a hang.
 
 namespace jb {
@@ -35,15 +36,18 @@ constexpr int OFF_K = OFF_Q + Q_BYTES;
 constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
 constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
 constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-// barriers: q_full, k_full[2], v_full[2], kv_free[2], s_full[2], p_ready[2], o_done[2]
-constexpr int NBAR = 1 + 6 * STAGES;
+// barriers: q_full, k_full[2], v_full[2], k_free[2], v_free[2], s_full[2], p_ready[2], o_done[2], xchg[2], xsum
+constexpr int NBAR = 2 + 8 * STAGES;
 constexpr int OFF_MISC = OFF_BAR + NBAR * 8;
-constexpr int SMEM = OFF_MISC + 16;
-constexpr int ALLOC = SMEM + 1024;
+constexpr int OFF_RED = OFF_MISC + 16;           // softmax exchange: maxima [2 tiles][2 halves][128 rows] (fp32)
+constexpr int SMEM = OFF_RED + 4 * 128 * 4;
+// the swizzled tiles need a 1024-byte aligned base; the dynamic shared memory of a kernel with no static shared
+// memory starts there, which the kernel checks (and reports through the status word instead of running misaligned)
+constexpr int ALLOC = SMEM;
 static_assert(ALLOC <= 227 * 1024, "shared memory");
 constexpr int TM_S = 0;                // S buffer b at column TM_S + 64 b
 constexpr int TM_O = 256;              // O at columns [256, 512)
-constexpr int THREADS = 6 * 32;
+constexpr int THREADS = 10 * 32;
 
 struct Params {
   const int* tables;
@@ -58,6 +62,14 @@ struct Params {
   int* err;
 };
 
+// 2^x by the hardware's approximate base-2 exponential (PTX ex2.approx.ftz.f32), as the reference's Triton
+// tl.exp2 does; -inf and very negative arguments give +0
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // K-major SW128 descriptor (rows of 128 B, 8-row groups 1024 B apart), as common.cuh's sw128_desc
 __device__ __forceinline__ uint64_t kmajor_desc(uint32_t saddr) { return sw128_desc(saddr); }
 // MN-major SW128 descriptor: rows (K direction) of 128 B = 64 N elements, 8-row groups SBO = 1024 B apart along K,
@@ -70,16 +82,23 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t saddr, uint32_t lbo) {
 __global__ void __launch_bounds__(THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_pool,
                      const __grid_constant__ CUtensorMap tm_kn, const __grid_constant__ CUtensorMap tm_vn, Params p) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = smem_raw;
+  if (smem_u32(smem) & 1023u) {   // uniform over the CTA: every thread returns before any barrier or allocation
+    if (threadIdx.x == 0 && p.err) atomicCAS(p.err, 0, JB_DEV_TIMEOUT | 99);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* q_full = bars;
   uint64_t* k_full = bars + 1;
   uint64_t* v_full = k_full + STAGES;
-  uint64_t* kv_free = v_full + STAGES;
-  uint64_t* s_full = kv_free + STAGES;
+  uint64_t* k_free = v_full + STAGES;     // a K tile is free once its Q K^T is done, a V tile once its P V is
+  uint64_t* v_free = k_free + STAGES;
+  uint64_t* s_full = v_free + STAGES;
   uint64_t* p_ready = s_full + 2;
   uint64_t* o_done = p_ready + 2;
+  uint64_t* xchg = o_done + 2;           // the 8 softmax warps' row maxima of tile j are in (by tile parity)
+  uint64_t* xsum_bar = xchg + 2;         // their row sums are in
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + OFF_MISC + 4);
 
@@ -97,11 +116,14 @@ __global__ void __launch_bounds__(THREADS, 1)
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&k_full[s], 1);
       mbar_init(&v_full[s], 1);
-      mbar_init(&kv_free[s], 1);
+      mbar_init(&k_free[s], 1);
+      mbar_init(&v_free[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&p_ready[s], 4);
+      mbar_init(&p_ready[s], 8);
       mbar_init(&o_done[s], 1);
+      mbar_init(&xchg[s], 8);
     }
+    mbar_init(xsum_bar, 8);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -126,31 +148,33 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int c = 0; c < 4; ++c)
           tma_load_3d(smem + OFF_Q + c * (128 * 128) + h * (BQ * 128), &tm_q, q_full, 64 * c, 4 * g + h,
                       tok0);
+      // the source rows of tile j's two 32-key halves: pool rows of the prefix pages (a page past the prefix's last
+      // reads the sink page: masked, its V rows zeroed), or rows of the new keys
+      auto load = [&](int j, bool values, uint8_t* dst, uint64_t* bar) {
+        for (int half = 0; half < 2; ++half) {
+          int r0;
+          const CUtensorMap* map;
+          if (j < pre_tiles) {
+            const int pi = 2 * j + half;
+            const int page = pi * PAGE < P ? p.tables[(size_t)row * p.table_stride + p.kv_entry + pi] : 0;
+            r0 = ((page * p.attn_layers + p.attn_layer) * 2 + (values ? 1 : 0)) * PAGE;
+            map = &tm_pool;
+          } else {
+            r0 = row * p.n + (j - pre_tiles) * BKN + half * PAGE;
+            map = values ? &tm_vn : &tm_kn;
+          }
+          for (int c = 0; c < 4; ++c) tma_load_3d(dst + c * (BKN * 128) + half * (PAGE * 128), map, bar, 64 * c, g, r0);
+        }
+      };
       for (int j = 0; j < tiles; ++j) {
         const int s = j % STAGES;
-        if (!mbar_wait(&kv_free[s], ((j / STAGES) & 1) ^ 1, abort_flag, p.err, 21)) break;
-        uint8_t* kd = smem + OFF_K + s * KV_BYTES;
-        uint8_t* vd = smem + OFF_V + s * KV_BYTES;
+        const uint32_t ph = ((j / STAGES) & 1) ^ 1;
+        if (!mbar_wait(&k_free[s], ph, abort_flag, p.err, 21)) break;
         mbar_arrive_expect_tx(&k_full[s], KV_BYTES);
+        load(j, false, smem + OFF_K + s * KV_BYTES, &k_full[s]);
+        if (!mbar_wait(&v_free[s], ph, abort_flag, p.err, 31)) break;
         mbar_arrive_expect_tx(&v_full[s], KV_BYTES);
-        for (int half = 0; half < 2; ++half) {     // 32 keys each
-          for (int c = 0; c < 4; ++c) {
-            uint8_t* kdst = kd + c * (BKN * 128) + half * (PAGE * 128);
-            uint8_t* vdst = vd + c * (BKN * 128) + half * (PAGE * 128);
-            if (j < pre_tiles) {
-              // page 2 j + half of the prefix (a page past the prefix's last reads the sink page: masked, V zeroed)
-              const int pi = 2 * j + half;
-              const int page = pi * PAGE < P ? p.tables[(size_t)row * p.table_stride + p.kv_entry + pi] : 0;
-              const int r0 = ((page * p.attn_layers + p.attn_layer) * 2) * PAGE;   // K rows; V rows + PAGE
-              tma_load_3d(kdst, &tm_pool, &k_full[s], 64 * c, g, r0);
-              tma_load_3d(vdst, &tm_pool, &v_full[s], 64 * c, g, r0 + PAGE);
-            } else {
-              const int k0 = (j - pre_tiles) * BKN + half * PAGE;   // new keys of this row
-              tma_load_3d(kdst, &tm_kn, &k_full[s], 64 * c, g, row * p.n + k0);
-              tma_load_3d(vdst, &tm_vn, &v_full[s], 64 * c, g, row * p.n + k0);
-            }
-          }
-        }
+        load(j, true, smem + OFF_V + s * KV_BYTES, &v_full[s]);
       }
     }
   } else if (warp == 1) {
@@ -175,6 +199,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                       idesc_s, kk != 0);
         }
         tc_commit(&s_full[j & 1]);
+        tc_commit(&k_free[s]);
         return true;
       };
       auto issue_o = [&](int j) -> bool {
@@ -188,7 +213,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int kk = 0; kk < BKN / 16; ++kk)
           tc_mma_bf16(tmem + TM_O, kmajor_desc(pa + 32 * kk), mnmajor_desc(va + kk * 16 * 128, BKN * 128), idesc_o,
                       (j | kk) != 0);
-        tc_commit(&kv_free[s]);   // K and V of the stage are read (this tile's Q K^T was issued before)
+        tc_commit(&v_free[s]);
         tc_commit(&o_done[j & 1]);
         return true;
       };
@@ -199,34 +224,39 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---------------- softmax + epilogue: thread = query row r = 32 h + i (tensor-memory lane)
+    // ---------------- softmax + epilogue: 8 warps, two per tensor-memory lane quadrant. Thread = query row r = 32 h
+    // + i (its lane) and one half of the row's scores (keys [32 half, + 32) of each tile) and of its O columns
+    // ([128 half, + 128)); the two halves' maxima meet through shared memory, their sums at the end.
     const int quad = warp & 3;
+    const int half = (warp - 2) >> 2;
     const int r = 32 * quad + lane;
     const int h = r >> 5, i = r & 31;
     const int tok = qb * BQ + i;                       // this row's new-token index within its row of the pass
     const uint32_t lane_bits = (uint32_t)(32 * quad) << 16;
+    float* xmax = reinterpret_cast<float*>(smem + OFF_RED);          // [2 tiles][2 halves][128 rows]
     float m = -1e30f, l = 0.f;
     bool ok = true;
     for (int j = 0; j < tiles && ok; ++j) {
       ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag, p.err, 26);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
-      uint32_t sa[32], sb[32];   // the tile's 64 scores of this row
-      tmem_ld32(tmem + lane_bits + TM_S + 64 * (j & 1), sa);
-      tmem_ld32(tmem + lane_bits + TM_S + 64 * (j & 1) + 32, sb);
+      uint32_t sv[32];   // this half's 32 scores of the row
+      tmem_ld32(tmem + lane_bits + TM_S + 64 * (j & 1) + 32 * half, sv);
       tc_wait_ld();
       const bool prefix = j < pre_tiles;
-      const int key0 = prefix ? j * BKN : (j - pre_tiles) * BKN;
-      const int limit = prefix ? P - key0 : tok + 1 - key0;   // keys [key0, key0 + limit) of the tile are valid
-      float mx = m;
+      const int key0 = (prefix ? j * BKN : (j - pre_tiles) * BKN) + 32 * half;
+      const int limit = prefix ? P - key0 : tok + 1 - key0;   // keys [key0, key0 + limit) of this half are valid
+      float mine = -1e30f;   // the max of the raw scores; scaled below (scale_log2 > 0 keeps the order)
 #pragma unroll
-      for (int c = 0; c < 32; ++c) {
-        const float xa = c < limit ? __uint_as_float(sa[c]) * p.scale_log2 : -1e30f;
-        const float xb = c + 32 < limit ? __uint_as_float(sb[c]) * p.scale_log2 : -1e30f;
-        sa[c] = __float_as_uint(xa);
-        sb[c] = __float_as_uint(xb);
-        mx = fmaxf(mx, fmaxf(xa, xb));
-      }
+      for (int c = 0; c < 32; ++c)
+        if (c < limit) mine = fmaxf(mine, __uint_as_float(sv[c]));
+      mine = mine > -1e30f ? mine * p.scale_log2 : -1e30f;
+      xmax[((j & 1) * 2 + half) * 128 + r] = mine;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&xchg[j & 1]);
+      ok = mbar_wait(&xchg[j & 1], (j >> 1) & 1, abort_flag, p.err, 32);   // both halves' maxima of tile j are in
+      if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
+      const float mx = fmaxf(m, fmaxf(mine, xmax[((j & 1) * 2 + (half ^ 1)) * 128 + r]));
       // P buffer j % 2 is free once the value product of tile j - 2 is done (o_done); O may be rescaled only after
       // the value product of tile j - 1
       if (j >= 1) {
@@ -239,15 +269,16 @@ __global__ void __launch_bounds__(THREADS, 1)
           tc_fence_after();
         }
         if (__any_sync(0xffffffffu, rescale)) {   // tensor-memory loads are warp-wide: the warp rescales together
-          const float alpha = rescale ? exp2f(m - mx) : 1.0f;
+          const float alpha = rescale ? ex2(m - mx) : 1.0f;
 #pragma unroll 1
-          for (int cc = 0; cc < HD / 32; ++cc) {
+          for (int cc = 0; cc < HD / 64; ++cc) {   // this half's 128 O columns
             uint32_t ov[32];
-            tmem_ld32(tmem + lane_bits + TM_O + 32 * cc, ov);
+            const uint32_t oa = tmem + lane_bits + TM_O + 128 * half + 32 * cc;
+            tmem_ld32(oa, ov);
             tc_wait_ld();
 #pragma unroll
             for (int e = 0; e < 32; ++e) ov[e] = __float_as_uint(__uint_as_float(ov[e]) * alpha);
-            w4t::tmem_st32(tmem + lane_bits + TM_O + 32 * cc, ov);
+            w4t::tmem_st32(oa, ov);
           }
           w4t::tc_wait_st();
           l *= alpha;
@@ -256,31 +287,32 @@ __global__ void __launch_bounds__(THREADS, 1)
       } else {
         m = mx;
       }
-      // P = bf16(exp2(s - m)) into the swizzled K-major P tile (row r: 64 keys = 128 B), the row sum unrounded
+      // P = bf16(exp2(s - m)) into the swizzled K-major P tile (row r: 64 keys = 128 B; this half's 4 chunks of 16
+      // B), this half's row sum unrounded
       uint8_t* pt = smem + OFF_P + (j & 1) * P_BYTES;
       float rs = 0.f;
 #pragma unroll
-      for (int c8 = 0; c8 < 8; ++c8) {
+      for (int c8 = 0; c8 < 4; ++c8) {
         float e8[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           const int c = 8 * c8 + e;
-          const uint32_t sv = c < 32 ? sa[c & 31] : sb[c & 31];
-          e8[e] = c < limit ? exp2f(__uint_as_float(sv) - m) : 0.f;
+          e8[e] = c < limit ? ex2(fmaf(__uint_as_float(sv[c]), p.scale_log2, -m)) : 0.f;
           rs += e8[e];
         }
-        *reinterpret_cast<uint4*>(pt + sw128_offset(r, c8)) =
+        *reinterpret_cast<uint4*>(pt + sw128_offset(r, 4 * half + c8)) =
             make_uint4(pack_bf2(e8[0], e8[1]), pack_bf2(e8[2], e8[3]), pack_bf2(e8[4], e8[5]), pack_bf2(e8[6], e8[7]));
       }
       l += rs;
-      if (prefix && P - key0 < BKN) {
+      const int tile_key0 = prefix ? j * BKN : 0;
+      if (prefix && P - tile_key0 < BKN) {
         // stale page contents past the prefix: zero those V rows (P is 0 there, but 0 x NaN is NaN)
         const int s = j % STAGES;
         ok = mbar_wait(&v_full[s], (j / STAGES) & 1, abort_flag, p.err, 28);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         uint8_t* vt = smem + OFF_V + s * KV_BYTES;
-        const int first = P - key0 > 0 ? P - key0 : 0;
-        for (int idx = r; idx < (BKN - first) * 4 * 8; idx += 128) {   // rows x 4 chunks x 8 pieces of 16 B
+        const int first = P - tile_key0 > 0 ? P - tile_key0 : 0;
+        for (int idx = threadIdx.x - 64; idx < (BKN - first) * 4 * 8; idx += 256) {   // rows x 4 chunks x 8 x 16 B
           const int key = first + idx / 32, rest = idx % 32, c = rest / 8, piece = rest % 8;
           *reinterpret_cast<uint4*>(vt + c * (BKN * 128) + key * 128 + piece * 16) = make_uint4(0, 0, 0, 0);
         }
@@ -290,7 +322,15 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_ready[j & 1]);
     }
-    // ---------------- epilogue: O / l -> bf16, times bf16(sigmoid(gate)) -> y
+    // ---------------- epilogue: O / l -> bf16, times bf16(sigmoid(gate)) -> y (this half's 128 columns). The two
+    // halves' sums meet in the exchange buffer of the parity the last tile did not use (its last reader, tile
+    // tiles - 2, finished before the last tile's barrier).
+    float* xsum = xmax + (tiles & 1) * 2 * 128;
+    xsum[half * 128 + r] = l;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(xsum_bar);
+    ok = ok && mbar_wait(xsum_bar, 0, abort_flag, p.err, 33);
+    l += xsum[(half ^ 1) * 128 + r];
     if (ok && tiles > 0) {
       const int jl = tiles - 1;
       ok = mbar_wait(&o_done[jl & 1], (jl >> 1) & 1, abort_flag, p.err, 29);
@@ -300,12 +340,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       const int t = tok0 + i;
       const int qh = 4 * g + h;
-      const __nv_bfloat16* gate = p.pr + (size_t)t * p.ldpr + qh * 2 * HD + HD;
-      __nv_bfloat16* yrow = p.y + (size_t)t * p.ldy + qh * HD;
+      const __nv_bfloat16* gate = p.pr + (size_t)t * p.ldpr + qh * 2 * HD + HD + 128 * half;
+      __nv_bfloat16* yrow = p.y + (size_t)t * p.ldy + qh * HD + 128 * half;
 #pragma unroll 1
-      for (int cc = 0; cc < HD / 32; ++cc) {
+      for (int cc = 0; cc < HD / 64; ++cc) {
         uint32_t ov[32];
-        tmem_ld32(tmem + lane_bits + TM_O + 32 * cc, ov);
+        tmem_ld32(tmem + lane_bits + TM_O + 128 * half + 32 * cc, ov);
         tc_wait_ld();
 #pragma unroll
         for (int q8 = 0; q8 < 4; ++q8) {

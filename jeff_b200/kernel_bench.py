@@ -205,16 +205,56 @@ def cfg3(reps: int) -> list[dict]:
              "bytes": layer_bytes, "unfused_ms": prep_ms + scan_ms + norm_ms}]
 
 
+def cfg4_attention(reps: int) -> list[dict]:
+    """Configuration 4's attention layer: 64 rows x 128 new tokens, each over its own 512-token prefix in pool pages;
+    the tcgen05 kernel with the gate fused, and the mma.sync kernel + gate_mul. FLOPs: Q K^T and P V over each query's
+    keys (the 512 prefix keys and its causal new keys); bytes: q, the new keys and values, the prefix pages' keys and
+    values of this layer, the gates and y."""
+    b, n, plen = 64, 128, 512
+    pool = PrefixPool(2 + b * (50 + plen // 32) + 4, "cuda")
+    slots = [pool.reserve(1, f"attention {r}", plen) for r in range(b)]
+    g = torch.Generator(device="cuda").manual_seed(4)
+    pool.kv.normal_(0.0, 1.0, generator=g)
+    tables = pool.tables.index_select(0, torch.tensor(slots, device="cuda")).contiguous()
+    pos = torch.full((b,), plen, dtype=torch.int32, device="cuda")
+    t = b * n
+    q = torch.randn(t, C.NQ, C.HD, generator=g, device="cuda").to(torch.bfloat16)
+    kn = torch.randn(t, C.NKV, C.HD, generator=g, device="cuda").to(torch.bfloat16)
+    vn = torch.randn(t, C.NKV, C.HD, generator=g, device="cuda").to(torch.bfloat16)
+    pr = torch.randn(t, C.ATTN_PROJ, generator=g, device="cuda").to(torch.bfloat16)
+    y = torch.empty(t, C.NQ * C.HD, dtype=torch.bfloat16, device="cuda")
+    ao = torch.empty(t, C.NQ, C.HD, dtype=torch.bfloat16, device="cuda")
+    tc_ms = timed(lambda: kernels.paged_attention_gated(q, pool, tables, 0, pos, kn, vn, n, pr, out=y), reps)
+
+    def old() -> None:
+        kernels.paged_attention(q, pool, tables, 0, pos, kn, vn, n, out=ao)
+        kernels.gate_mul(ao, pr, out=y)
+
+    old_ms = timed(old, reps)
+    keys = b * C.NQ * sum(plen + i + 1 for i in range(n))          # (query, key) pairs
+    flops = 4 * keys * C.HD
+    bytes_ = t * C.NQ * C.HD * 2 * 3 + 2 * t * C.NKV * C.HD * 2 + b * plen * 2 * C.NKV * C.HD * 2
+    config = "cfg4 attention: 64 rows x 128 new tokens over 512-token prefixes"
+    return [{"kernel": "attention_kernel (tcgen05, gate fused)", "config": config, "ms": tc_ms, "bytes": bytes_,
+             "flops": flops},
+            {"kernel": "paged_attention_kernel (mma.sync) + gate_mul_kernel", "config": config, "ms": old_ms,
+             "bytes": bytes_, "flops": flops}]
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--only", choices=["cfg1", "cfg2", "cfg3", "attention"], default=None)
     args = ap.parse_args()
     if not torch.cuda.is_available():
         raise SystemExit("kernel_bench needs a CUDA GPU")
     torch.cuda.set_device(0)
     peak, source = hbm_peak()
     tpeak, tsource = tensor_peak()
-    for line in [cfg1(args.reps), *cfg2(args.reps), *cfg3(args.reps)]:
+    runs = {"cfg1": lambda: [cfg1(args.reps)], "cfg2": lambda: cfg2(args.reps), "cfg3": lambda: cfg3(args.reps),
+            "attention": lambda: cfg4_attention(args.reps)}
+    chosen = [args.only] if args.only else list(runs)
+    for line in [x for name in chosen for x in runs[name]()]:
         gbs = line["bytes"] / (line["ms"] / 1e3) / 1e9
         line.update(gbs=gbs, hbm_peak_gbs=peak, peak_source=source, frac=gbs / peak)
         if "flops" in line:
