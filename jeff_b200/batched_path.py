@@ -83,7 +83,14 @@ class Workspace:
 
 class BatchedPath:
     def __init__(self, fast: FastPath, tokenize: Callable[[str], list[int]] | None = None,
-                 max_tokens: int = C.MAX_PASS_TOKENS, max_rows_per_pass: int = max(C.BATCH_BUCKETS)) -> None:
+                 max_tokens: int = C.MAX_PASS_TOKENS, max_rows_per_pass: int = max(C.BATCH_BUCKETS),
+                 batch_buckets: Sequence[int] = C.BATCH_BUCKETS) -> None:
+        # the row counts decide() pads a decision pass to (one recorded graph per bucket and new-token bucket): the
+        # reference's 1, 2, 4, ..., 64 by default; a deployment may record fewer (configuration 5: 1, 8, 16, 32, 64)
+        if sorted(batch_buckets) != list(batch_buckets) or batch_buckets[0] != 1 or \
+                batch_buckets[-1] != max(C.BATCH_BUCKETS):
+            raise ValueError(f"batch buckets {list(batch_buckets)}: increasing, from 1 to {max(C.BATCH_BUCKETS)}")
+        self.batch_buckets = tuple(batch_buckets)
         self.fast = fast
         self.pool = fast.prefixes
         # the Gated DeltaNet mixer: three launches (jb_gdn_prep_rows, jb_gdn_scan, jb_gated_norm) by default, or the
@@ -281,9 +288,11 @@ class BatchedPath:
         return self.prefix_graphs[(b, nb)]
 
     def record(self, shapes: Sequence[tuple[int, int]] | None = None) -> float:
-        """Record the decision graphs of `shapes` (every PASS_SHAPES shape the workspace holds by default)."""
+        """Record the decision graphs of `shapes` (by default every PASS_SHAPES shape of this path's batch buckets that
+        the workspace holds)."""
         started = time.perf_counter()
-        for b, n in shapes if shapes is not None else [s for s in PASS_SHAPES if s[0] * s[1] <= self.max_tokens]:
+        default = [s for s in PASS_SHAPES if s[0] * s[1] <= self.max_tokens and s[0] in self.batch_buckets]
+        for b, n in shapes if shapes is not None else default:
             self.graph(b, n)
         torch.cuda.synchronize(self.device)
         return time.perf_counter() - started
@@ -443,7 +452,7 @@ class BatchedPath:
             cap = min(max_rows(n), self.ws.rows, self.max_tokens // n)
             for first in range(0, len(members), cap):
                 part = members[first:first + cap]
-                plan.append((next(bb for bb in C.BATCH_BUCKETS if bb >= len(part)), n, part))
+                plan.append((next(bb for bb in self.batch_buckets if bb >= len(part)), n, part))
         done = self.run_passes([(b, n, [rows[i] for i in part], [lengths[i] for i in part]) for b, n, part in plan])
         for (_, n, part), (probs, ms) in zip(plan, done, strict=True):
             timing["model_ms"] += ms

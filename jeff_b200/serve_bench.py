@@ -13,7 +13,7 @@ _binding_key and EngineRouter.predict), so one prefix's states live on one GPU. 
 the reference scheduler's rule (runtime/python/src/jeff_runtime/scheduler.py, Scheduler._gather): a micro-batch
 closes `window_ms` after its oldest waiting call arrived, or as soon as `max_batch_rows` calls wait, and takes at
 most `max_batch_rows` calls in arrival order; the batch goes to B200Engine.predict_many as one group per adapter,
-which runs it as graph replays per new-token bucket in batch buckets of 1 to 64 rows. A call's latency is the time
+which runs it as graph replays per new-token bucket in the configuration's batch buckets of 1, 8, 16, 32 and 64 rows. A call's latency is the time
 from its arrival to the end of the engine call that answered it. The reference's defaults are window 1 ms, 64 rows
 (docs/operating.md: --batch-window-ms 1 --max-batch-rows 64).
 
@@ -40,6 +40,7 @@ from dataclasses import dataclass
 import numpy as np
 
 ADAPTERS, PREFIXES, PREFIX_TOKENS = 32, 64, 512
+CFG5_BATCH_BUCKETS = (1, 8, 16, 32, 64)   # the configuration's CUDA-graph batch buckets
 MEAN_NEW, SIGMA_NEW, MAX_NEW = 96.0, 0.8, 1024
 
 
@@ -218,7 +219,8 @@ def build_engine(rank: int, world: int, pool_prefixes: int):
     fast = FastPath(model, max_adapters=ADAPTERS, base_readout=synthetic.base_head(model) if not skeleton else None,
                     pool_pages_count=2 + pool_prefixes * (50 + PREFIX_TOKENS // 32) + 64)
     ids = prefix_ids()
-    engine = B200Engine(paths=(fast, BatchedPath(fast, tokenize=lambda text: ids[text])), max_adapters=ADAPTERS)
+    path = BatchedPath(fast, tokenize=lambda text: ids[text], batch_buckets=CFG5_BATCH_BUCKETS)
+    engine = B200Engine(paths=(fast, path), max_adapters=ADAPTERS)
     for a in range(1, ADAPTERS + 1):
         engine.add_adapter(adapter_id(a), synthetic.make_adapter(model, a, seed=1000 + a, skeleton=skeleton))
     if world > 1:

@@ -29,7 +29,7 @@ def fake_path(prefix_len: int = 10, rows_cap: int = 64, max_tokens: int = C.MAX_
         return out
 
     path = SimpleNamespace(_check=lambda rows: [prefix_len] * len(rows), run_passes=run_passes,
-                           ws=SimpleNamespace(rows=rows_cap), max_tokens=max_tokens)
+                           ws=SimpleNamespace(rows=rows_cap), max_tokens=max_tokens, batch_buckets=C.BATCH_BUCKETS)
     return path, calls
 
 
@@ -64,3 +64,17 @@ def test_decide_cuts_a_bucket_into_passes_of_at_most_max_rows() -> None:
     path, calls = fake_path(rows_cap=8)                        # a smaller workspace caps the passes too
     BatchedPath.decide(path, rows_of([30] * 20))
     assert [(b, len(ids)) for b, _, ids in calls[0]] == [(8, 8), (8, 8), (4, 4)]
+
+
+def test_a_path_with_the_configuration_5_batch_buckets_pads_to_them() -> None:
+    """batch_buckets (1, 8, 16, 32, 64), the serving configuration's graph buckets: 5 rows of one new-token bucket run
+    as one pass of 8 rows, 20 as one of 32; a bucket list that does not run from 1 to 64 is refused."""
+    import pytest
+
+    path, calls = fake_path()
+    path.batch_buckets = (1, 8, 16, 32, 64)
+    BatchedPath.decide(path, rows_of([20] * 5))
+    BatchedPath.decide(path, rows_of([20] * 20))
+    assert [b for b, _, _ in calls[0]] == [8] and [b for b, _, _ in calls[1]] == [32]
+    with pytest.raises(ValueError, match="from 1 to 64"):
+        BatchedPath(SimpleNamespace(), batch_buckets=(8, 16, 64))   # type: ignore[arg-type]
