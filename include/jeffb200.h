@@ -150,6 +150,14 @@ int jb_gdn_scan(const uint16_t* q, const uint16_t* k, const uint16_t* v, const f
                 uint16_t* o, int b, int n, void* pool, int64_t page_bytes, const int32_t* tables, int table_stride,
                 int first_head, int heads_per_page, const int32_t* last, const int32_t* out_tables,
                 int out_table_stride, void* stream);
+/* The same rule with every chunk product on tcgen05 (M 128 MMAs, S and the chunk products in tensor memory, two
+ * CTAs per SM), arguments and results as jb_gdn_scan (the same bf16 rounding points; fp32 sums in the tensor core's
+ * order): the decision and prefix passes' scan. Replaces fla's chunk_gated_delta_rule at batched_path.py:282-288,
+ * :322-324. */
+int jb_gdn_scan_tc(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g, const uint16_t* beta,
+                   uint16_t* o, int b, int n, void* pool, int64_t page_bytes, const int32_t* tables, int table_stride,
+                   int first_head, int heads_per_page, const int32_t* last, const int32_t* out_tables,
+                   int out_table_stride, void* stream);
 /* The same rule token by token in fp32 (one value column per thread pair): the reference's
  * batched_kernels.gdn_recurrent_slots (:200-261); last (nullable) stops after last[r], zeros past it. */
 int jb_gdn_scan_recurrent(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,

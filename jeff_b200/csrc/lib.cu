@@ -115,6 +115,7 @@ int make_tmap_planes(CUtensorMap* map, const void* base, uint64_t rows, uint32_t
 #include "elementwise.cu"
 #include "gdn.cu"
 #include "gdn_chunk.cu"
+#include "gdn_tc.cu"
 #include "attention.cu"
 #include "attention_tc.cu"
 

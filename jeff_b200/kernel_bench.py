@@ -183,7 +183,8 @@ def cfg3(reps: int) -> list[dict]:
     o = torch.empty_like(outs[2])
     prep_ms = timed(lambda: kernels.gdn_prep_rows(pr, pool, tables, 0, conv_w, a_neg, dt_bias, n, outs=outs), reps)
     q, k, v, gg, beta = outs
-    scan_ms = timed(lambda: kernels.gdn_scan(q, k, v, gg, beta, pool, tables, 0, out=o), reps)
+    scan_ms = timed(lambda: kernels.gdn_scan(q, k, v, gg, beta, pool, tables, 0, out=o, kernel="tc"), reps)
+    chunk_ms = timed(lambda: kernels.gdn_scan(q, k, v, gg, beta, pool, tables, 0, out=o, kernel="chunk"), reps)
     gnorm = torch.ones(C.DV, dtype=torch.bfloat16, device="cuda")
     y = torch.empty(t, C.NV * C.DV, dtype=torch.bfloat16, device="cuda")
     norm_ms = timed(lambda: kernels.gated_norm(o.view(t, C.NV, C.DV), pr, gnorm, out=y), reps)
@@ -198,7 +199,9 @@ def cfg3(reps: int) -> list[dict]:
     layer_bytes = t * C.GDN_PROJ * 2 + tails + states + t * C.NV * C.DV * 2
     config = "cfg3 64 rows x 256 tokens"
     return [{"kernel": "gdn prep_kernel", "config": config, "ms": prep_ms, "bytes": prep_bytes},
-            {"kernel": "gdn chunk_kernel (scan from pooled state)", "config": config, "ms": scan_ms,
+            {"kernel": "gdn scan_kernel (tcgen05 chunk scan from pooled state)", "config": config, "ms": scan_ms,
+             "bytes": scan_bytes},
+            {"kernel": "gdn chunk_kernel (mma.sync chunk scan from pooled state)", "config": config, "ms": chunk_ms,
              "bytes": scan_bytes},
             {"kernel": "gated_norm_kernel", "config": config, "ms": norm_ms, "bytes": norm_bytes},
             {"kernel": "gdn layer_kernel (prep + scan + gated norm fused)", "config": config, "ms": layer_ms,

@@ -199,9 +199,11 @@ def gdn_prep_rows(pr: torch.Tensor, pool, tables: torch.Tensor, gdn_layer: int, 
 def gdn_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor, beta: torch.Tensor, pool,
              tables: torch.Tensor, gdn_layer: int, last: torch.Tensor | None = None,
              out_tables: torch.Tensor | None = None, out: torch.Tensor | None = None,
-             kernel: str = "chunk") -> torch.Tensor:
-    """The gated delta rule from each row's pooled state; o (B, n, 16, 128). kernel "chunk" (64-token chunks on
-    tensor cores, fla's chunk_gated_delta_rule) or "recurrent" (token by token, batched_kernels.gdn_recurrent_slots)."""
+             kernel: str = "tc") -> torch.Tensor:
+    """The gated delta rule from each row's pooled state; o (B, n, 16, 128). kernel "tc" (64-token chunks, every
+    chunk product a tcgen05 MMA with the state in tensor memory: fla's chunk_gated_delta_rule), "chunk" (the same
+    chunks on mma.sync, the form the fused jb_gdn_layer shares bit for bit) or "recurrent" (token by token,
+    batched_kernels.gdn_recurrent_slots)."""
     b, n = q.shape[:2]
     shapes = pool.shapes
     if tables.dim() != 2 or tables.shape[0] < b or tables.shape[1] < shapes.fixed_pages or tables.dtype != torch.int32:
@@ -211,7 +213,7 @@ def gdn_scan(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, g: torch.Tensor,
         if not x.is_contiguous():
             raise ValueError(f"gdn_scan: {name} must be contiguous")
     o = out if out is not None else torch.empty_like(v)
-    name = {"chunk": "jb_gdn_scan", "recurrent": "jb_gdn_scan_recurrent"}[kernel]
+    name = {"tc": "jb_gdn_scan_tc", "chunk": "jb_gdn_scan", "recurrent": "jb_gdn_scan_recurrent"}[kernel]
     _lib.call(name, ptr(q), ptr(k), ptr(v), ptr(g), ptr(beta), ptr(o), b, n, ptr(pool.data),
               shapes.page_bytes, ptr(tables), tables.stride(0), shapes.state[0] * gdn_layer, shapes.heads_per_page,
               ptr(last), ptr(out_tables), 0 if out_tables is None else out_tables.stride(0), stream_ptr())

@@ -467,7 +467,7 @@ def gdn_inputs(b: int, n: int, seed: int):
     return q, k, v, gg, beta
 
 
-@pytest.mark.parametrize("kernel", ["chunk", "recurrent"])
+@pytest.mark.parametrize("kernel", ["tc", "chunk", "recurrent"])
 @pytest.mark.parametrize("b", BATCHES)
 @pytest.mark.parametrize("n", [32, 64, 160])
 @pytest.mark.parametrize("gdn_layer", [0, 5, 17])
@@ -495,10 +495,10 @@ def test_gdn_scan_matches_the_oracle(pool_fixture, kernel: str, b: int, n: int, 
         assert not stopped[r, end:].any()
 
 
-@pytest.mark.parametrize("kernel", ["chunk", "recurrent"])
+@pytest.mark.parametrize("kernel", ["tc", "chunk", "recurrent"])
 def test_gdn_scan_writes_the_final_state_into_the_output_pages(pool_fixture, kernel: str) -> None:
-    """The prefix pass's final states: the recurrent kernel within float32 noise (rtol 1e-4); the chunk kernel,
-    whose state products take bf16 operands, within 1e-2 norm-wise per head."""
+    """The prefix pass's final states: the recurrent kernel within float32 noise (rtol 1e-4); the two chunk kernels
+    (tcgen05 and mma.sync), whose state products take bf16 operands, within 1e-2 norm-wise per head."""
     pool, slots, states = pool_fixture
     b, n = 3, 160
     ss = [slots[33], 0, slots[100]]
@@ -533,10 +533,13 @@ def gdn_layer_weights(seed: int):
 
 
 def three_kernels(pr, pool, tables, gdn_layer, conv_w, a_neg, dt_bias, gnorm, n, last=None, real=None,
-                  out_tables=None):
+                  out_tables=None, scan="chunk"):
+    """jb_gdn_prep_rows, jb_gdn_scan (the mma.sync chunk form, which jb_gdn_layer shares bit for bit, unless `scan`
+    names another) and jb_gated_norm in sequence."""
     q, k, v, g, beta = kernels.gdn_prep_rows(pr, pool, tables, gdn_layer, conv_w, a_neg, dt_bias, n, real=real,
                                              out_tables=out_tables)
-    o = kernels.gdn_scan(q, k, v, g, beta, pool, tables, gdn_layer, last=last, out_tables=out_tables)
+    o = kernels.gdn_scan(q, k, v, g, beta, pool, tables, gdn_layer, last=last, out_tables=out_tables,
+                         kernel=scan)
     return kernels.gated_norm(o.view(-1, C.NV, C.DV), pr, gnorm)
 
 
@@ -598,8 +601,10 @@ def test_gdn_layer_prefix_mode_writes_the_same_pages(pool_fixture) -> None:
                 pool.release(slot)
 
 
-def test_gdn_layer_at_configuration_3_matches_the_oracle() -> None:
-    """Configuration 3 as specified: 64 rows x 256 new tokens, each from a pooled fp32 state ~ N(0, 0.1) of 16 heads
+@pytest.mark.parametrize("path", ["fused", "tc"])
+def test_gdn_layer_at_configuration_3_matches_the_oracle(path: str) -> None:
+    """path "fused": jb_gdn_layer; "tc": jb_gdn_prep_rows, the tcgen05 scan and jb_gated_norm (the pass's three
+    launches). Configuration 3 as specified: 64 rows x 256 new tokens, each from a pooled fp32 state ~ N(0, 0.1) of 16 heads
     of 128 x 128 and a cached conv tail ~ N(0, 1); raw q | k | v ~ N(0, 1) bf16 through the width-4 conv (weights
     ~ N(0, 0.5)), SiLU and the L2 norm; beta = sigmoid(N(0, 1)); g = logsigmoid(N(2, 0.5)) (A_log = 0, dt_bias = 0,
     a = -N(2, 0.5), so -exp(A_log) softplus(a + dt_bias) = logsigmoid(-a)); z ~ N(0, 1). The fused layer's y
@@ -628,8 +633,12 @@ def test_gdn_layer_at_configuration_3_matches_the_oracle() -> None:
     pr[:, C.QKV_DIM + C.Z_DIM + C.NV:] = -(2.0 + 0.5 * torch.randn(b * n, C.NV, generator=g))
     pr = pr.to(torch.bfloat16).cuda()
     real = torch.full((b,), n, dtype=torch.int32).cuda()
-    y = kernels.gdn_layer(pr, shapes_pool, tables, gdn_layer, conv_w.cuda(), torch.full((C.NV,), -1.0).cuda(),
-                          dt_bias.cuda(), gnorm.cuda(), n, real=real, out_tables=out_tables)
+    args = (pr, shapes_pool, tables, gdn_layer, conv_w.cuda(), torch.full((C.NV,), -1.0).cuda(), dt_bias.cuda(),
+            gnorm.cuda(), n)
+    if path == "fused":
+        y = kernels.gdn_layer(*args, real=real, out_tables=out_tables)
+    else:
+        y = three_kernels(*args, real=real, out_tables=out_tables, scan="tc").view(b * n, C.NV * C.DV)
     torch.cuda.synchronize()
     worst_y, worst_s = 0.0, 0.0
     for r in range(b):
@@ -646,7 +655,8 @@ def test_gdn_layer_at_configuration_3_matches_the_oracle() -> None:
         fin = shapes_pool.gather(outs[r])[1][gdn_layer]
         for hh in range(C.NV):
             worst_s = max(worst_s, model_ref.rel_error(fin[hh], s_fin[0][hh]))
-    print(f"configuration 3: worst per-(row, head) relative error of y {worst_y:.2e}, of the final state {worst_s:.2e}")
+    print(f"configuration 3 ({path}): worst per-(row, head) relative error of y {worst_y:.2e}, of the final state "
+          f"{worst_s:.2e}")
     assert worst_y < 1e-2
     assert worst_s < 1e-2
 
