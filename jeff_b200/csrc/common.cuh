@@ -32,6 +32,11 @@ int* device_status_word();   // this device's status word (static device memory)
 // Encodes a 2-D tiled tensor map (driver entry point fetched through the runtime; no libcuda link needed).
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner, uint64_t outer,
                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle);
+// Encodes a tiled tensor map of rank 1..5: dims[i] elements, strides[i] bytes between consecutive indices of
+// dimension i + 1 (multiples of 16), box[i] elements per copy. Out-of-range elements of a load read as zero; a store
+// skips them.
+int make_tmap_nd(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
+                 const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swizzle);
 // A bf16 matrix (rows, cols) with 16-byte rows pieces, viewed as planes of 8 columns: dims {8, rows, cols / 8},
 // strides {row_bytes, 16}, box {8, box_rows, cols / 8}. One load lands as cols / 8 planes of box_rows x 16 B each
 // (the planes layout of planes_desc). Returns JB_OK, or an error status (with jb_last_error set) when the driver
@@ -132,6 +137,20 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
       : "memory");
 }
+__device__ __forceinline__ void tma_load_4d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1, int c2,
+                                            int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, const void* src, int c0, int c1, int c2, int c3) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(src))
+               : "memory");
+}
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void* src, int c0, int c1) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
@@ -150,6 +169,18 @@ __device__ __forceinline__ void tma_store_wait_read() {
 __device__ __forceinline__ void tma_store_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ------------------------------------------------------------------ device: one lane of a warp
+
+// true in exactly one active lane of the (converged) warp: the lane that issues a warp's single-thread operations
+// while the whole warp keeps computing their operands, which stay warp-uniform
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n elect.sync _|p, 0xffffffff;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // ------------------------------------------------------------------ device: tcgen05 (5th-generation tensor cores)

@@ -109,6 +109,40 @@ int make_tmap_planes(CUtensorMap* map, const void* base, uint64_t rows, uint32_t
   return JB_OK;
 }
 
+int make_tmap_nd(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
+                 const uint64_t* strides, const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  auto fn = encode_fn();
+  if (!fn) {
+    set_error("cuTensorMapEncodeTiled is not available from the driver");
+    return JB_ECUDA;
+  }
+  if (rank < 1 || rank > 5 || (reinterpret_cast<uintptr_t>(base) & 15)) {
+    set_error("tensor map: rank %d, base %p (16-byte aligned, rank 1..5)", rank, base);
+    return JB_EINVAL;
+  }
+  cuuint64_t d[5], st[4];
+  cuuint32_t b[5], elem[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    elem[i] = 1;
+    if (i + 1 < rank) {
+      st[i] = strides[i];
+      if (strides[i] & 15) {
+        set_error("tensor map: stride %d of %llu bytes is not a multiple of 16", i, (unsigned long long)strides[i]);
+        return JB_EINVAL;
+      }
+    }
+  }
+  CUresult r = fn(map, dtype, (cuuint32_t)rank, const_cast<void*>(base), d, st, b, elem, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("cuTensorMapEncodeTiled failed (%d) for a rank-%d map", (int)r, rank);
+    return JB_ECUDA;
+  }
+  return JB_OK;
+}
+
 }  // namespace jb
 
 #include "w4a16_gemm.cu"

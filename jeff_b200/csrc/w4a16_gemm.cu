@@ -96,7 +96,9 @@ struct Layout {
   static constexpr int OFF_ADP = OFF_MISC + 16;
   static constexpr int MAX_ROWS = 512;            // adapter indices staged in shared memory (M / row_len rows)
   static constexpr int OFF_MASK = OFF_ADP + MAX_ROWS * 4;
-  static constexpr int BYTES = OFF_MASK + MAX_MASK_TILES * MASK_WORDS * 4;
+  static constexpr int OFF_STG = OFF_MASK + MAX_MASK_TILES * MASK_WORDS * 4;   // epilogue staging, 32 tokens
+  static constexpr int STG_PITCH = BN + 8;                                         // bf16 elements per token row
+  static constexpr int BYTES = OFF_STG + 32 * STG_PITCH * 2;
   static constexpr int ALLOC = BYTES + 1024;       // room to align the base to 1024 B
   static_assert(ALLOC <= 227 * 1024, "shared memory");
 };
@@ -148,7 +150,9 @@ __device__ __forceinline__ int mask_nth(const uint32_t* mask, int j) {
   return 0;
 }
 
-__device__ __forceinline__ float silu_rounded(float g) { return round_bf(g / (1.0f + expf(-g))); }
+// silu(g) rounded to bf16, by the fast exponential and division intrinsics (their error, a few fp32 units in the last
+// place, moves the rounded value by one bf16 step only when it lies that close to a rounding boundary)
+__device__ __forceinline__ float silu_rounded(float g) { return round_bf(__fdividef(g, 1.0f + __expf(-g))); }
 
 template <bool ZERO>
 __global__ void __launch_bounds__(THREADS, 1)
@@ -300,27 +304,32 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else if (warp == 1) {
-    // ---------------- MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_bf16(HM, BN);
+    // ---------------- MMA issuer: the whole warp runs the loop and computes the (warp-uniform) descriptors; one
+    // elected lane issues the MMAs and commits
+    {
+      // swap AB: the dequantised weights are A (M = 128 columns), the tokens B (N = 256 rows), so one MMA per K16
+      // step covers the whole 256 x 128 tile and reads the weight tile once
+      constexpr uint32_t idesc = idesc_bf16(BN, BM);
+      constexpr uint32_t idesc_half = idesc_bf16(BN, HM);
+      const bool issuer = elect_one();
       uint32_t kg = 0;
       int it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++it) {
         const int b = it & 1;
-        ok = mbar_wait(&tmem_empty[b], ((it >> 1) & 1) ^ 1, abort_flag, p.err, 2);
+        ok = __all_sync(0xffffffffu, mbar_wait(&tmem_empty[b], ((it >> 1) & 1) ^ 1, abort_flag, p.err, 2));
         if (!ok) break;
         tc_fence_after();
-        const uint32_t acc = tmem + b * 2 * BN;
+        const uint32_t acc = tmem + b * BM;
         const int nkt = nkb + lora_blocks(tile % p.m_tiles);
         for (int kb = 0; kb < nkt; ++kb, ++kg) {
           const int s = kg % STAGES;
           const uint32_t ph = (kg / STAGES) & 1;
           // one wait: the dequantisers arrive on deq[s] only after each of them saw full[s] complete (the stage's
           // TMA bytes landed), so deq[s] covers both
-          ok = mbar_wait(&deq[s], ph, abort_flag, p.err, 4);
+          ok = __all_sync(0xffffffffu, mbar_wait(&deq[s], ph, abort_flag, p.err, 4));
           if (!ok) break;
-          JB_STAGE(4, kg);
+          if (issuer) JB_STAGE(4, kg);
           tc_fence_after();
           if (kb >= nkb && lora_tma) {
             // each half against its own adapter, planes layout: K16 step j reads planes 2j, 2j + 1
@@ -328,25 +337,28 @@ __global__ void __launch_bounds__(THREADS, 1)
             for (int h = h_lo; h < h_hi; ++h) {
               const uint32_t xa = smem_u32(smem + L::OFF_X + s * L::X_BYTES + (h - h_lo) * (HM * 128));
               const uint32_t wa = smem_u32(smem + L::OFF_W + s * L::W_BYTES + (h - h_lo) * (p.rank / 8) * 2048);
-              for (int j = 0; j < p.rank / 16; ++j)
-                tc_mma_bf16(acc + h * BN, planes_desc(xa + 2 * j * 2048, 2048), planes_desc(wa + 2 * j * 2048, 2048),
-                            idesc, 1);
+              for (int j = 0; j < p.rank / 16; ++j) {   // the half's 128 tokens are accumulator columns [128 h, +128)
+                const uint64_t ad = planes_desc(wa + 2 * j * 2048, 2048), bd = planes_desc(xa + 2 * j * 2048, 2048);
+                if (issuer) tc_mma_bf16(acc + h * HM, ad, bd, idesc_half, 1);
+              }
             }
           } else {
-            const uint64_t a0 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES));
-            const uint64_t a1 = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES + HM * 128));
-            const uint64_t bd = sw128_desc(smem_u32(smem + L::OFF_W + s * L::W_BYTES));
+            const uint64_t ad = sw128_desc(smem_u32(smem + L::OFF_W + s * L::W_BYTES));
+            const uint64_t bd = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES));
+            if (issuer) {
 #pragma unroll
-            for (int kk = 0; kk < BK / 16; ++kk) {
-              tc_mma_bf16(acc, a0 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
-              tc_mma_bf16(acc + BN, a1 + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+              for (int kk = 0; kk < BK / 16; ++kk) tc_mma_bf16(acc, ad + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
             }
           }
-          tc_commit(&empty[s]);
-          JB_STAGE(5, kg);
+          if (issuer) {
+            tc_commit(&empty[s]);
+            JB_STAGE(5, kg);
+          }
+          __syncwarp();
         }
         if (!ok) break;
-        tc_commit(&tmem_full[b]);
+        if (issuer) tc_commit(&tmem_full[b]);
+        __syncwarp();
       }
     }
   } else if (warp < 2 + DEQ_WARPS) {
@@ -430,10 +442,13 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---------------- epilogue: 128 threads; thread = row lrow of both halves (its TMEM lane); direct stores
+    // ---------------- epilogue: 128 threads; thread = output column n of the tile (its TMEM lane), the accumulator's
+    // 256 columns the tile's tokens. 32 tokens at a time: TMEM -> bf16 -> a [token][column] staging tile in shared
+    // memory -> whole 16-byte pieces of each token's row to y (row-contiguous stores)
     const int et = threadIdx.x - 64 - DEQ_WARPS * 32;
-    const int lrow = 32 * (warp & 3) + lane;
+    const int n = 32 * (warp & 3) + lane;
     const uint32_t lane_bits = (uint32_t)(32 * (warp & 3)) << 16;
+    __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + L::OFF_STG);
     __nv_bfloat16* y = p.y;
     const int ow = p.swiglu ? p.out / 2 : p.out;      // output columns
     int it = 0;
@@ -445,67 +460,51 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (!*epi_ok) break;
       if (et == 0) JB_STAGE(6, it);
       tc_fence_after();
-      const uint32_t acc = tmem + b * 2 * BN + lane_bits;
+      const uint32_t acc = tmem + b * BM + lane_bits;
 #pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        const int gm = m0 + h * HM + lrow;
-        __nv_bfloat16* yrow = y + (size_t)gm * p.ldy;
-        if (!p.swiglu) {
-#pragma unroll 1
-          for (int c = 0; c < BN / 32; ++c) {
-            uint32_t r[32];
-            tmem_ld32(acc + h * BN + c * 32, r);
-            tc_wait_ld();
-            if (gm < p.M) {
+      for (int t0 = 0; t0 < BM; t0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(acc + t0, r);
+        tc_wait_ld();
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int col = n0 + c * 32 + q * 8;
-                if (col < ow) {
-                  uint4 v;
-                  v.x = pack_bf2(__uint_as_float(r[8 * q + 0]), __uint_as_float(r[8 * q + 1]));
-                  v.y = pack_bf2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]));
-                  v.z = pack_bf2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]));
-                  v.w = pack_bf2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]));
-                  *reinterpret_cast<uint4*>(yrow + col) = v;
-                }
-              }
-            }
+        for (int e = 0; e < 32; ++e) stg[e * L::STG_PITCH + n] = f2bf(__uint_as_float(r[e]));
+        if (t0 + 32 == BM) {
+          // the accumulator is read: release it to the MMA issuer for the tile after next
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tmem_empty[b]);
+        }
+        named_barrier(2, EPI_WARPS * 32);
+        if (!p.swiglu) {
+#pragma unroll
+          for (int i = et; i < 32 * (BN / 8); i += EPI_WARPS * 32) {
+            const int tt = i / (BN / 8), c8 = i % (BN / 8);
+            const int gm = m0 + t0 + tt, col = n0 + 8 * c8;
+            if (gm < p.M && col < ow)
+              *reinterpret_cast<uint4*>(y + (size_t)gm * p.ldy + col) =
+                  *reinterpret_cast<const uint4*>(stg + tt * L::STG_PITCH + 8 * c8);
           }
         } else {
-#pragma unroll 1
-          for (int c = 0; c < 2; ++c) {
-            uint32_t rg[32], ru[32];
-            tmem_ld32(acc + h * BN + c * 32, rg);
-            tmem_ld32(acc + h * BN + 64 + c * 32, ru);
-            tc_wait_ld();
-            if (gm < p.M) {
+          // columns 0-63 of the tile are gate, 64-127 the matching up columns: 64 outputs bf16(bf16(silu(g)) u)
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                const int col = n0 / 2 + c * 32 + q * 8;
-                float o[8];
+          for (int i = et; i < 32 * (BN / 16); i += EPI_WARPS * 32) {
+            const int tt = i / (BN / 16), c8 = i % (BN / 16);
+            const int gm = m0 + t0 + tt, col = n0 / 2 + 8 * c8;
+            if (gm < p.M && col < ow) {
+              const uint4 gv = *reinterpret_cast<const uint4*>(stg + tt * L::STG_PITCH + 8 * c8);
+              const uint4 uv = *reinterpret_cast<const uint4*>(stg + tt * L::STG_PITCH + BN / 2 + 8 * c8);
+              const uint32_t* gw = &gv.x;
+              const uint32_t* uw = &uv.x;
+              uint32_t ov[4];
 #pragma unroll
-                for (int e = 0; e < 8; ++e) {
-                  const float g = round_bf(__uint_as_float(rg[8 * q + e]));
-                  const float u = round_bf(__uint_as_float(ru[8 * q + e]));
-                  o[e] = silu_rounded(g) * u;
-                }
-                if (col < ow) {
-                  uint4 v;
-                  v.x = pack_bf2(o[0], o[1]);
-                  v.y = pack_bf2(o[2], o[3]);
-                  v.z = pack_bf2(o[4], o[5]);
-                  v.w = pack_bf2(o[6], o[7]);
-                  *reinterpret_cast<uint4*>(yrow + col) = v;
-                }
-              }
+              for (int e = 0; e < 4; ++e)
+                ov[e] = pack_bf2(silu_rounded(bf_lo(gw[e])) * bf_lo(uw[e]), silu_rounded(bf_hi(gw[e])) * bf_hi(uw[e]));
+              *reinterpret_cast<uint4*>(y + (size_t)gm * p.ldy + col) = make_uint4(ov[0], ov[1], ov[2], ov[3]);
             }
           }
         }
+        named_barrier(2, EPI_WARPS * 32);
       }
-      // the accumulator is read: release it to the MMA issuer for the tile after next
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tmem_empty[b]);
       if (et == 0) JB_STAGE(7, it);
     }
   }
