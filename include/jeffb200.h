@@ -85,6 +85,21 @@ int jb_int4_lora_product(const uint16_t* x, int m, int k, const int32_t* words, 
                          const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
                          uint16_t* mid, uint16_t* y, int ldy, int flags, void* stream);
 
+/* jb_int4_lora_product for passes too small to fill the GPU (the reference's small batch buckets, B * N down to 32
+ * tokens): when the pass's 256 x 128 tiles are fewer than the SMs, each tile's K blocks are split into equal slices
+ * (at least two blocks each, at most twice the SM count of work items), each slice a work item; the slices' fp32
+ * sums go to `partials` (the caller's scratch, partial_floats floats: slices x columns rounded up to 128 x m rounded
+ * up to 32), and the CTA whose slice arrives last adds them in slice order (deterministic) and stores y. `counters`
+ * (counter_count int32, one per tile) must be zero before the first call; every call leaves them zero. Too little
+ * scratch or too many tiles: the unsplit product. Same result as jb_int4_lora_product up to the order of the fp32
+ * sums. Replaces int4_kernels.int4_product (int4_kernels.py:132-177) in the reference's batch-1 and small-batch
+ * graphs. */
+int jb_int4_lora_product_split(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
+                               const uint16_t* zeros, int group, int columns, int out, const uint16_t* lora_a,
+                               const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
+                               uint16_t* mid, uint16_t* y, int ldy, int flags, float* partials,
+                               int64_t partial_floats, int32_t* counters, int counter_count, void* stream);
+
 /* jb_int4_lora_product without the `mid` argument, allocating nothing: the shrink's output goes to a scratch array
  * fixed in the library's device memory (one per device, m * rank <= JB_PRODUCT_STATIC_MID_MAX; larger calls get
  * JB_EINVAL). For callers that must not allocate device memory: a host binding the C ABI directly with no device

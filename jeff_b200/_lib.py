@@ -86,7 +86,7 @@ def call(name: str, *args) -> None:
     global launches
     lib = load()
     if name not in _NO_LAUNCH:
-        products = ("jb_int4_lora_product", "jb_int4_lora_product_static")
+        products = ("jb_int4_lora_product", "jb_int4_lora_product_static", "jb_int4_lora_product_split")
         launches += 2 if (name in products and args[11]) else 1   # args[11]: rank
     status = getattr(lib, name)(*args)
     if status != 0:

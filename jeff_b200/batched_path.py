@@ -49,6 +49,10 @@ def max_rows(n: int) -> int:
     return max(b for b in C.BATCH_BUCKETS if b * n <= C.MAX_PASS_TOKENS)
 
 
+SPLIT_FLOATS = 8 * 2**20     # 32 MB: the slices of a 512-token pass's widest product
+SPLIT_COUNTERS = 4096
+
+
 class Workspace:
     """Every intermediate tensor of a pass of up to `tokens` tokens and `rows` rows."""
 
@@ -74,6 +78,10 @@ class Workspace:
         self.vn = e(tokens, C.NKV, C.HD)
         self.act = e(tokens, C.INTER)
         self.mid = e(tokens * max(max_rank, 16))
+        # split-K scratch of small passes' products (jb_int4_lora_product_split): fp32 slice sums and per-tile
+        # counters, which start at zero and are left at zero by every product
+        self.split = (torch.empty(SPLIT_FLOATS, dtype=torch.float32, device=device),
+                      torch.zeros(SPLIT_COUNTERS, dtype=torch.int32, device=device))
         self.tables = torch.zeros(rows, width, dtype=torch.int32, device=device)
         self.zero_tables = torch.zeros(rows, width, dtype=torch.int32, device=device)
         self.zero_pos = torch.zeros(rows, dtype=torch.int32, device=device)
@@ -99,6 +107,18 @@ class BatchedPath:
         # instructions then run inside the scan's one 8-warp CTA per SM, which issues on 30% of cycles (latency
         # bound), where the separate prep kernel runs them at full occupancy. So the pass keeps the three launches.
         self.fused_gdn = False
+        # the chunk scan of decision passes and of prefix passes: "tc" (tcgen05, the default), "chunk" (mma.sync) or
+        # "recurrent" (token by token in fp32, no bf16 operands inside the rule)
+        self.gdn_scan_kernel = "tc"
+        # prefix states are cached and every later call on the prefix starts from them, so the prefix pass computes
+        # them with the fp32 rule (no bf16 operands inside the chunk products; 1.5x the tcgen05 scan's prefix-pass
+        # time, measured on a B200): on the 1,024 chained calls of configuration 4 this takes the decision/abstain
+        # outcomes identical to the oracle's from 1,022 to 1,023 (both remaining differences within 0.01 of the
+        # 0.8 threshold)
+        self.gdn_prefix_scan_kernel = "recurrent"
+        # split-K products for passes too small to fill the GPU (jb_int4_lora_product_split): measured slower than
+        # the unsplit product on batch-1 passes, so off
+        self.split_k = False
         # attention: the tcgen05 kernel with the output gate fused (jb_paged_attention_gated); False runs the mma.sync
         # kernel and jb_gate_mul (the same result within the attention tolerance, tested)
         self.tc_attention = True
@@ -170,7 +190,7 @@ class BatchedPath:
             layer = f.layers[li]
             _, h = kernels.add_rms(x, d, layer["norm_in"], xo=x, h=ws.h[:t])
             proj = layer["proj"]
-            pr = proj(h, adapters, n, ws.mid, ws.pr[:t * proj.out].view(t, proj.out))
+            pr = proj(h, adapters, n, ws.mid, ws.pr[:t * proj.out].view(t, proj.out), split=ws.split if self.split_k else None)
             if layer["kind"] == "linear_attention" and self.fused_gdn:
                 y = kernels.gdn_layer(pr, pool, gdn_tables, gi, layer["conv"], layer["a_neg"], layer["dt_bias"],
                                       layer["gnorm"], n, last=last, real=real, out_tables=out_tables,
@@ -185,6 +205,7 @@ class BatchedPath:
                                                          layer["dt_bias"], n, real=real, out_tables=out_tables,
                                                          outs=outs)
                 o = kernels.gdn_scan(q, k, v, g, beta, pool, gdn_tables, gi, last=last, out_tables=out_tables,
+                                     kernel=self.gdn_prefix_scan_kernel if prefix else self.gdn_scan_kernel,
                                      out=ws.o[:size].view(b, n, C.NV, C.DV))
                 y = kernels.gated_norm(o, pr, layer["gnorm"], out=ws.y[:t, :C.NV * C.DV])
                 gi += 1
@@ -203,10 +224,10 @@ class BatchedPath:
                     ao = kernels.paged_attention(aq, pool, attn_tables, ai, pos, kn, vn, n, out=ws.ao[:t])
                     y = kernels.gate_mul(ao, pr, out=ws.y[:t])
                 ai += 1
-            d = layer["out"](y, adapters, n, ws.mid, ws.d[:t])
+            d = layer["out"](y, adapters, n, ws.mid, ws.d[:t], split=ws.split if self.split_k else None)
             _, h = kernels.add_rms(x, d, layer["norm_post"], xo=x, h=ws.h[:t])
-            act = layer["mlp_in"](h, adapters, n, ws.mid, ws.act[:t])     # SwiGLU in the product's epilogue
-            d = layer["mlp_down"](act, adapters, n, ws.mid, ws.d[:t])
+            act = layer["mlp_in"](h, adapters, n, ws.mid, ws.act[:t], split=ws.split if self.split_k else None)     # SwiGLU in the product's epilogue
+            d = layer["mlp_down"](act, adapters, n, ws.mid, ws.d[:t], split=ws.split if self.split_k else None)
             if trace is not None:
                 trace.append((x.float() + d.float()).to(DT))
         return d

@@ -145,6 +145,7 @@ int make_tmap_nd(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
 
 }  // namespace jb
 
+#include "lora_shrink_tc.cu"
 #include "w4a16_gemm.cu"
 #include "elementwise.cu"
 #include "gdn.cu"

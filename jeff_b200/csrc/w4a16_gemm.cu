@@ -43,12 +43,20 @@ namespace w4 {
 // each dequantiser warp arrived, 12..15 each dequantiser warp saw the stage full. jb_stage_trace_read copies it out.
 // Without JB_TRACE the stamps compile to nothing.
 #ifdef JB_TRACE
+__device__ unsigned long long g_prod_trace[6][256];
+#define JB_PROD(ev, kg)                                                                    \
+  do {                                                                                     \
+    if (blockIdx.x == 0 && (unsigned)(kg) < 256u) g_prod_trace[ev][kg] = clock64();        \
+  } while (0)
 __device__ unsigned long long g_stage_trace[16][256];
 #define JB_STAGE(ev, kg)                                                                   \
   do {                                                                                     \
     if (blockIdx.x == 0 && (unsigned)(kg) < 256u) g_stage_trace[ev][kg] = clock64();       \
   } while (0)
 #else
+#define JB_PROD(ev, kg) \
+  do {                  \
+  } while (0)
 #define JB_STAGE(ev, kg) \
   do {                   \
   } while (0)
@@ -78,7 +86,19 @@ struct Params {
   int ldy;
   int* err;
   int planes3d;                  // 1: tm_mid / tm_lb load every plane of a half at once; 0: one plane per load
+  int x_rows;                    // rows of tm_x's box: min(256, M rounded up to 16)
+  // split K: each tile's K blocks in k_split equal slices, each slice a work item of its own. A slice writes its
+  // fp32 sums to partials ([slice][column][token], ldp tokens per column), then bumps counters[tile]; the CTA whose
+  // slice arrives last adds the slices in slice order (deterministic), rounds and stores y, and resets the counter
+  int k_split;
+  float* partials;
+  int* counters;
+  int ldp;
 };
+
+// the MMA's N for a tile's tokens from m0: its real tokens rounded up to 16, at most `cap` (small passes multiply
+// only the rows they have)
+__device__ __forceinline__ int tile_tokens(int M, int m0, int cap) { return min(cap, ((M - m0 + 15) >> 4) << 4); }
 
 struct Layout {
   static constexpr int X_BYTES = BM * BK * 2;      // 32 KB: two 128-row swizzled tiles back to back
@@ -184,6 +204,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const bool gathered = has_lora && !lora_tma;
   const bool halves_together = 2 * p.rank <= BK;
   const int tiles = p.m_tiles * p.n_tiles;
+  const int S = p.k_split;                 // K slices per tile (1: none)
+  const int items = tiles * S;             // work items (tile, slice), the slice fastest
+  const int kbs = nkb / S;                 // base K blocks of one item
   int* s_adp = reinterpret_cast<int*>(smem + L::OFF_ADP);
   uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem + L::OFF_MASK);   // [m tile][MASK_WORDS]
   if (lora_tma) {
@@ -258,27 +281,34 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) {
     // ---------------- producer
     if (lane == 0) {
-      const uint32_t bytes = L::X_BYTES + L::RAW_BYTES + L::SC_BYTES * (ZERO ? 2 : 1);
+      const uint32_t bytes = p.x_rows * BK * 2 + L::RAW_BYTES + L::SC_BYTES * (ZERO ? 2 : 1);
       uint32_t kg = 0;
-      for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+      for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
+        const int tile = item / S, ks = item % S;
         const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
-        const int nkt = nkb + lora_blocks(tile % p.m_tiles);
+        const int nkt = kbs + (ks == S - 1 ? lora_blocks(tile % p.m_tiles) : 0);
         for (int kb = 0; kb < nkt; ++kb, ++kg) {
           const int s = kg % STAGES;
           if (!mbar_wait(&empty[s], ((kg / STAGES) & 1) ^ 1, abort_flag, p.err, 1)) break;
           JB_STAGE(0, kg);
-          if (kb < nkb) {
+          if (kb < kbs) {
+            const int kgl = ks * kbs + kb;   // the K block in the whole product
             mbar_arrive_expect_tx(&full[s], bytes);
-            tma_load_2d(smem + L::OFF_X + s * L::X_BYTES, &tm_x, &full[s], kb * BK, m0);
-            tma_load_2d(smem + L::OFF_RAW + s * L::RAW_BYTES, &tm_w, &full[s], n0, kb * (BK / 8));
-            tma_load_2d(smem + L::OFF_SC + s * L::SC_BYTES, &tm_s, &full[s], n0, (kb * BK) / p.group);
-            if (ZERO) tma_load_2d(smem + L::OFF_ZR + s * L::SC_BYTES, &tm_z, &full[s], n0, (kb * BK) / p.group);
+            JB_PROD(0, kg);
+            tma_load_2d(smem + L::OFF_X + s * L::X_BYTES, &tm_x, &full[s], kgl * BK, m0);
+            JB_PROD(1, kg);
+            tma_load_2d(smem + L::OFF_RAW + s * L::RAW_BYTES, &tm_w, &full[s], n0, kgl * (BK / 8));
+            JB_PROD(2, kg);
+            tma_load_2d(smem + L::OFF_SC + s * L::SC_BYTES, &tm_s, &full[s], n0, (kgl * BK) / p.group);
+            JB_PROD(3, kg);
+            if (ZERO) tma_load_2d(smem + L::OFF_ZR + s * L::SC_BYTES, &tm_z, &full[s], n0, (kgl * BK) / p.group);
+            JB_PROD(4, kg);
             JB_STAGE(1, kg);
           } else if (lora_tma) {
             // a LoRA block by TMA: for each of its halves, the half's mid rows (rank / 8 planes of 128 rows x 16 B)
             // into the x slot and its adapter's B rows for this column tile into the weight slot. Rows past m and
             // an invalid adapter read outside the tensors: zeros.
-            const int h_lo = halves_together ? 0 : kb - nkb, h_hi = halves_together ? 2 : h_lo + 1;
+            const int h_lo = halves_together ? 0 : kb - kbs, h_hi = halves_together ? 2 : h_lo + 1;
             const int planes = p.rank / 8;
             mbar_arrive_expect_tx(&full[s], 2 * (h_hi - h_lo) * planes * 2048);
             for (int h = h_lo; h < h_hi; ++h) {
@@ -309,19 +339,20 @@ __global__ void __launch_bounds__(THREADS, 1)
     {
       // swap AB: the dequantised weights are A (M = 128 columns), the tokens B (N = 256 rows), so one MMA per K16
       // step covers the whole 256 x 128 tile and reads the weight tile once
-      constexpr uint32_t idesc = idesc_bf16(BN, BM);
-      constexpr uint32_t idesc_half = idesc_bf16(BN, HM);
       const bool issuer = elect_one();
       uint32_t kg = 0;
       int it = 0;
       bool ok = true;
-      for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x, ++it) {
+      for (int item = blockIdx.x; item < items && ok; item += gridDim.x, ++it) {
+        const int tile = item / S, ks = item % S;
         const int b = it & 1;
         ok = __all_sync(0xffffffffu, mbar_wait(&tmem_empty[b], ((it >> 1) & 1) ^ 1, abort_flag, p.err, 2));
         if (!ok) break;
         tc_fence_after();
         const uint32_t acc = tmem + b * BM;
-        const int nkt = nkb + lora_blocks(tile % p.m_tiles);
+        const int m0 = (tile % p.m_tiles) * BM;
+        const uint32_t idesc_tile = idesc_bf16(BN, tile_tokens(p.M, m0, BM));
+        const int nkt = kbs + (ks == S - 1 ? lora_blocks(tile % p.m_tiles) : 0);
         for (int kb = 0; kb < nkt; ++kb, ++kg) {
           const int s = kg % STAGES;
           const uint32_t ph = (kg / STAGES) & 1;
@@ -331,15 +362,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (!ok) break;
           if (issuer) JB_STAGE(4, kg);
           tc_fence_after();
-          if (kb >= nkb && lora_tma) {
+          if (kb >= kbs && lora_tma) {
             // each half against its own adapter, planes layout: K16 step j reads planes 2j, 2j + 1
-            const int h_lo = halves_together ? 0 : kb - nkb, h_hi = halves_together ? 2 : h_lo + 1;
+            const int h_lo = halves_together ? 0 : kb - kbs, h_hi = halves_together ? 2 : h_lo + 1;
             for (int h = h_lo; h < h_hi; ++h) {
+              if (m0 + h * HM >= p.M) continue;   // a half past the pass's tokens adds nothing
+              const uint32_t idesc_h = idesc_bf16(BN, tile_tokens(p.M, m0 + h * HM, HM));
               const uint32_t xa = smem_u32(smem + L::OFF_X + s * L::X_BYTES + (h - h_lo) * (HM * 128));
               const uint32_t wa = smem_u32(smem + L::OFF_W + s * L::W_BYTES + (h - h_lo) * (p.rank / 8) * 2048);
               for (int j = 0; j < p.rank / 16; ++j) {   // the half's 128 tokens are accumulator columns [128 h, +128)
                 const uint64_t ad = planes_desc(wa + 2 * j * 2048, 2048), bd = planes_desc(xa + 2 * j * 2048, 2048);
-                if (issuer) tc_mma_bf16(acc + h * HM, ad, bd, idesc_half, 1);
+                if (issuer) tc_mma_bf16(acc + h * HM, ad, bd, idesc_h, 1);
               }
             }
           } else {
@@ -347,7 +380,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint64_t bd = sw128_desc(smem_u32(smem + L::OFF_X + s * L::X_BYTES));
             if (issuer) {
 #pragma unroll
-              for (int kk = 0; kk < BK / 16; ++kk) tc_mma_bf16(acc, ad + 2 * kk, bd + 2 * kk, idesc, (kb | kk) != 0);
+              for (int kk = 0; kk < BK / 16; ++kk)
+                tc_mma_bf16(acc, ad + 2 * kk, bd + 2 * kk, idesc_tile, (kb | kk) != 0);
             }
           }
           if (issuer) {
@@ -368,10 +402,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     const int n = et & (BN - 1);            // this thread's weight column
     uint32_t kg = 0;
     bool ok = true;
-    for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+    for (int item = blockIdx.x; item < items && ok; item += gridDim.x) {
+      const int tile = item / S, ks = item % S;
       const int mt = tile % p.m_tiles;
       const int m0 = mt * BM, n0 = (tile / p.m_tiles) * BN;
-      const int nkt = nkb + lora_blocks(mt);
+      const int nkt = kbs + (ks == S - 1 ? lora_blocks(mt) : 0);
       for (int kb = 0; kb < nkt; ++kb, ++kg) {
         if ((int)(kg % GROUPS) != grp) continue;
         const int s = kg % STAGES;
@@ -380,7 +415,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         if (lane == 0) JB_STAGE(12 + ((et >> 5) & 3), kg);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         uint8_t* wt = smem + L::OFF_W + s * L::W_BYTES;
-        if (kb < nkb) {
+        if (kb < kbs) {
           const int32_t* raw = reinterpret_cast<const int32_t*>(smem + L::OFF_RAW + s * L::RAW_BYTES);
           const __nv_bfloat16* sc = reinterpret_cast<const __nv_bfloat16*>(smem + L::OFF_SC + s * L::SC_BYTES);
           const __nv_bfloat16* zr =
@@ -400,7 +435,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           // so their latencies overlap.
           const uint32_t* mask = s_mask + mt * MASK_WORDS;
           const int ke = mask_count(mask) * p.rank;    // expand columns of this tile
-          const int col0 = (kb - nkb) * BK;
+          const int col0 = (kb - kbs) * BK;
           const int lrow = n;
           const int gn = n0 + n;
           uint4 v[8];
@@ -451,8 +486,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem + L::OFF_STG);
     __nv_bfloat16* y = p.y;
     const int ow = p.swiglu ? p.out / 2 : p.out;      // output columns
+    volatile int* last_slice = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 12);
     int it = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++it) {
+    for (int item = blockIdx.x; item < items; item += gridDim.x, ++it) {
+      const int tile = item / S, ks = item % S;
       const int m0 = (tile % p.m_tiles) * BM, n0 = (tile / p.m_tiles) * BN;
       const int b = it & 1;
       if (et == 0) *epi_ok = mbar_wait(&tmem_full[b], (it >> 1) & 1, abort_flag, p.err, 6) ? 1 : 0;
@@ -461,19 +498,11 @@ __global__ void __launch_bounds__(THREADS, 1)
       if (et == 0) JB_STAGE(6, it);
       tc_fence_after();
       const uint32_t acc = tmem + b * BM + lane_bits;
-#pragma unroll 1
-      for (int t0 = 0; t0 < BM; t0 += 32) {
-        uint32_t r[32];
-        tmem_ld32(acc + t0, r);
-        tc_wait_ld();
+      const int t_end = min(BM, ((p.M - m0 + 31) >> 5) << 5);   // the tile's token chunks that hold tokens
+      // 32 tokens t0 .. of column n (fp32 bits in r) -> bf16 staging -> y, by the staging tile
+      auto emit = [&](int t0, const uint32_t (&r)[32]) {
 #pragma unroll
         for (int e = 0; e < 32; ++e) stg[e * L::STG_PITCH + n] = f2bf(__uint_as_float(r[e]));
-        if (t0 + 32 == BM) {
-          // the accumulator is read: release it to the MMA issuer for the tile after next
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(&tmem_empty[b]);
-        }
         named_barrier(2, EPI_WARPS * 32);
         if (!p.swiglu) {
 #pragma unroll
@@ -504,6 +533,64 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         named_barrier(2, EPI_WARPS * 32);
+      };
+      // this slice's partial sums of column n (split K only): [slice][column][token]
+      float* part = S > 1 ? p.partials + ((size_t)ks * p.n_tiles * BN + n0 + n) * p.ldp + m0 : nullptr;
+#pragma unroll 1
+      for (int t0 = 0; t0 < t_end; t0 += 32) {
+        uint32_t r[32];
+        tmem_ld32(acc + t0, r);
+        tc_wait_ld();
+        if (t0 + 32 == t_end) {
+          // the accumulator is read: release it to the MMA issuer for the tile after next
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tmem_empty[b]);
+        }
+        if (S == 1) {
+          emit(t0, r);
+        } else {
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(part + t0 + 4 * q) =
+                make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                            __uint_as_float(r[4 * q + 3]));
+        }
+      }
+      if (S > 1) {
+        // the last slice of the tile to arrive adds the slices in order and stores y
+        __threadfence();
+        named_barrier(2, EPI_WARPS * 32);
+        if (et == 0) *last_slice = atomicAdd(&p.counters[tile], 1) == S - 1 ? 1 : 0;
+        named_barrier(2, EPI_WARPS * 32);
+        if (*last_slice) {
+          __threadfence();
+          const float* col_parts = p.partials + (size_t)(n0 + n) * p.ldp + m0;
+          const size_t slice_stride = (size_t)p.n_tiles * BN * p.ldp;
+#pragma unroll 1
+          for (int t0 = 0; t0 < t_end; t0 += 32) {
+            float sum[32];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(col_parts + t0 + 4 * q));
+              sum[4 * q] = v.x; sum[4 * q + 1] = v.y; sum[4 * q + 2] = v.z; sum[4 * q + 3] = v.w;
+            }
+#pragma unroll 1
+            for (int k2 = 1; k2 < S; ++k2) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                const float4 v =
+                    __ldcg(reinterpret_cast<const float4*>(col_parts + k2 * slice_stride + t0 + 4 * q));
+                sum[4 * q] += v.x; sum[4 * q + 1] += v.y; sum[4 * q + 2] += v.z; sum[4 * q + 3] += v.w;
+              }
+            }
+            uint32_t r[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(sum[e]);
+            emit(t0, r);
+          }
+          if (et == 0) p.counters[tile] = 0;   // ready for the next launch
+        }
       }
       if (et == 0) JB_STAGE(7, it);
     }
@@ -769,8 +856,8 @@ int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ts, 
   if (e != cudaSuccess) return status_of(e, "w4a16: cudaFuncSetAttribute");
   e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return status_of(e, "w4a16: SM count");
-  const int tiles = p.m_tiles * p.n_tiles;
-  const int grid = tiles < sms ? tiles : sms;
+  const int items = p.m_tiles * p.n_tiles * p.k_split;
+  const int grid = items < sms ? items : sms;
   kernel<<<grid, THREADS, Layout::ALLOC, stream>>>(tx, tw, ts, tz, tm, tl, p);
   return check_launch("w4a16_lora_kernel");
 }
@@ -818,6 +905,14 @@ extern "C" int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* l
   auto ab = reinterpret_cast<const __nv_bfloat16*>(lora_a);
   auto mb = reinterpret_cast<__nv_bfloat16*>(mid);
   cudaStream_t st = (cudaStream_t)stream;
+  // the tcgen05 shrink (lora_shrink_tc.cu) for the pools the fast path builds (at most 256 rows); the mma.sync
+  // kernels below for larger pools
+  if (pool_rows <= lsh::MAX_POOL_ROWS && rank % 16 == 0 && rank >= 16 && rank <= 64) {
+    JB_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(lora_a) |
+                 reinterpret_cast<uintptr_t>(mid)) & 15) == 0,
+               "jb_lora_shrink: x, lora_a and mid must be 16-byte aligned");
+    return lsh::launch(xb, m, k, ab, rank, pool_rows, adapters, row_len, mb, st);
+  }
   if (k % w4::SH_BK == 0) {
     switch (rank) {
       case 16: return w4::launch_shrink_staged<2>(xb, m, k, ab, pool_rows, adapters, row_len, mb, st);
@@ -842,10 +937,14 @@ extern "C" int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* l
   return check_launch("lora_shrink_kernel");
 }
 
-extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
-                             const uint16_t* zeros, int group, int columns, int out, const uint16_t* mid,
-                             const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
-                             uint16_t* y, int ldy, int flags, void* stream) {
+namespace jb {
+namespace w4 {
+// jb_w4a16_lora with split K: k_split slices per tile (1: none), partials and counters the caller's scratch
+static int w4a16_lora_impl(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
+                           const uint16_t* zeros, int group, int columns, int out, const uint16_t* mid,
+                           const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
+                           uint16_t* y, int ldy, int flags, int k_split, float* partials, int32_t* counters,
+                           void* stream) {
   const bool swiglu = (flags & JB_PRODUCT_SWIGLU) != 0;
   const int yw = swiglu ? out / 2 : out;   // output columns
   JB_REQUIRE(x && words && scales && y, "jb_w4a16_lora: null pointer");
@@ -888,7 +987,9 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
   CUtensorMap tx, tw, ts, tz, tm, tl;
   int st;
   constexpr int BN = w4::BN;
-  if ((st = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, m, (uint64_t)k * 2, 64, w4::BM,
+  // small passes load only the rows they have: the box is the pass's tokens rounded up to 16, at most a tile
+  const int x_rows = m < w4::BM ? ((m + 15) / 16) * 16 : w4::BM;
+  if ((st = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, m, (uint64_t)k * 2, 64, x_rows,
                          CU_TENSOR_MAP_SWIZZLE_128B)))
     return st;
   if ((st = make_tmap_2d(&tw, words, CU_TENSOR_MAP_DATA_TYPE_INT32, columns, k / 8, (uint64_t)columns * 4, BN, 8,
@@ -930,15 +1031,29 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
                lora ? reinterpret_cast<const __nv_bfloat16*>(mid) : nullptr,
                reinterpret_cast<const __nv_bfloat16*>(lora_b), adapters, lora ? rank : 0, row_len > 0 ? row_len : 128,
                pool_rows, swiglu ? 1 : 0, (m + w4::BM - 1) / w4::BM, (columns + BN - 1) / BN,
-               reinterpret_cast<__nv_bfloat16*>(y), ldy, device_status_word(), planes3d};
+               reinterpret_cast<__nv_bfloat16*>(y), ldy, device_status_word(), planes3d, x_rows,
+               k_split, partials, counters, ((m + 31) / 32) * 32};
   if (zeros) return w4::launch<true>(tx, tw, ts, tz, tm, tl, p, (cudaStream_t)stream);
   return w4::launch<false>(tx, tw, ts, tz, tm, tl, p, (cudaStream_t)stream);
+}
+}  // namespace w4
+}  // namespace jb
+
+extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
+                             const uint16_t* zeros, int group, int columns, int out, const uint16_t* mid,
+                             const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
+                             uint16_t* y, int ldy, int flags, void* stream) {
+  return w4::w4a16_lora_impl(x, m, k, words, scales, zeros, group, columns, out, mid, lora_b, rank, pool_rows,
+                             adapters, row_len, y, ldy, flags, 1, nullptr, nullptr, stream);
 }
 
 #ifdef JB_TRACE
 // Measurement builds only (python -m jeff_b200.build --trace, libjeffb200_trace.so): copies the shared-memory
 // product kernel's stage trace, 16 x 256 clock64() stamps of CTA 0's hand-offs in its last launch, to `out`. Not
 // part of the product library or its header.
+extern "C" int jb_prod_trace_read(uint64_t* out) {
+  return status_of(cudaMemcpyFromSymbol(out, w4::g_prod_trace, sizeof(w4::g_prod_trace)), "jb_prod_trace_read");
+}
 extern "C" int jb_stage_trace_read(uint64_t* out) {
   JB_REQUIRE(out, "jb_stage_trace_read: null pointer");
   return status_of(cudaMemcpyFromSymbol(out, w4::g_stage_trace, sizeof(w4::g_stage_trace)),
@@ -965,6 +1080,62 @@ extern "C" int jb_int4_lora_product(const uint16_t* x, int m, int k, const int32
   }
   return jb_w4a16_lora(x, m, k, words, scales, zeros, group, columns, out, rank > 0 ? mid : nullptr, lora_b, rank,
                        pool_rows, adapters, row_len, y, ldy, flags, stream);
+}
+
+// The product with the base product's K split over several CTAs for passes too small to fill the GPU (their
+// tiles fewer than the SMs): each tile's K blocks in equal slices, at least two blocks each, as many slices as keep
+// the work items within twice the SM count and the partials within the caller's scratch. Same result as
+// jb_int4_lora_product up to the order of the fp32 sums (slices added in slice order: deterministic).
+extern "C" int jb_int4_lora_product_split(const uint16_t* x, int m, int k, const int32_t* words,
+                                          const uint16_t* scales, const uint16_t* zeros, int group, int columns,
+                                          int out, const uint16_t* lora_a, const uint16_t* lora_b, int rank,
+                                          int pool_rows, const int32_t* adapters, int row_len, uint16_t* mid,
+                                          uint16_t* y, int ldy, int flags, float* partials, int64_t partial_floats,
+                                          int32_t* counters, int counter_count, void* stream) {
+  JB_REQUIRE(partials && counters, "jb_int4_lora_product_split: null scratch");
+  JB_REQUIRE((reinterpret_cast<uintptr_t>(partials) & 15) == 0, "jb_int4_lora_product_split: partials alignment");
+  JB_REQUIRE(k > 0 && k % 64 == 0 && m > 0 && columns > 0, "jb_int4_lora_product_split: m %d, k %d, columns %d", m,
+             k, columns);
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int kb = k / 64;
+  if (rank > 0) {
+    JB_REQUIRE(mid && lora_a && adapters, "jb_int4_lora_product_split: LoRA needs lora_a, adapters and mid");
+    // the shrink split the same way when its 128-token tiles are fewer than the SMs (the same scratch: the shrink
+    // is done with it, and its counters back at zero, before the product starts on the stream)
+    const int mt = (m + lsh::TM - 1) / lsh::TM;
+    int shrink_split = 1;
+    if (pool_rows <= lsh::MAX_POOL_ROWS && rank % 16 == 0 && rank >= 16 && rank <= 64 && row_len > 0 && mt < sms &&
+        mt <= counter_count &&
+        ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(lora_a) | reinterpret_cast<uintptr_t>(mid)) &
+         15) == 0) {
+      for (int s = kb / 2; s >= 2; --s)
+        if (kb % s == 0 && mt * s <= 2 * sms && (int64_t)s * mt * lsh::TM * rank <= partial_floats) {
+          shrink_split = s;
+          break;
+        }
+    }
+    int st = shrink_split > 1
+                 ? lsh::launch(reinterpret_cast<const __nv_bfloat16*>(x), m, k,
+                               reinterpret_cast<const __nv_bfloat16*>(lora_a), rank, pool_rows, adapters, row_len,
+                               reinterpret_cast<__nv_bfloat16*>(mid), (cudaStream_t)stream, shrink_split, partials,
+                               counters)
+                 : jb_lora_shrink(x, m, k, lora_a, rank, pool_rows, adapters, row_len, mid, stream);
+    if (st) return st;
+  }
+  const int tiles = ((m + w4::BM - 1) / w4::BM) * ((columns + w4::BN - 1) / w4::BN);
+  const int64_t ldp = ((m + 31) / 32) * 32;
+  const int64_t per_slice = (int64_t)((columns + w4::BN - 1) / w4::BN) * w4::BN * ldp;
+  int split = 1;
+  if (!(flags & JB_PRODUCT_TMEM_A) && tiles < sms && tiles <= counter_count) {
+    for (int s = kb / 2; s >= 2; --s)
+      if (kb % s == 0 && tiles * s <= 2 * sms && s * per_slice <= partial_floats) {
+        split = s;
+        break;
+      }
+  }
+  return w4::w4a16_lora_impl(x, m, k, words, scales, zeros, group, columns, out, rank > 0 ? mid : nullptr, lora_b,
+                             rank, pool_rows, adapters, row_len, y, ldy, flags, split, partials, counters, stream);
 }
 
 // ------------------------------------------------------------------ the product without caller scratch

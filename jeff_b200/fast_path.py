@@ -80,11 +80,13 @@ class DeviceLin:
             self.lora_b[row].zero_()
 
     def __call__(self, x: torch.Tensor, adapters: torch.Tensor, row_len: int, mid: torch.Tensor | None,
-                 y: torch.Tensor | None = None) -> torch.Tensor:
+                 y: torch.Tensor | None = None, split: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
+        """y = the group's product of x with each token's adapter; `split` (fp32 slices, int32 counters): the
+        split-K scratch that lets a pass too small to fill the GPU spread each tile's K over several CTAs."""
         m = x.shape[0]
         mid_v = mid[:m * self.rank].view(m, self.rank) if (mid is not None and self.rank) else None
         return kernels.int4_product(x, self.words, self.scales, self.zeros, self.group, self.out, self.lora_a,
-                                    self.lora_b, adapters, row_len, mid_v, y, swiglu=self.swiglu)
+                                    self.lora_b, adapters, row_len, mid_v, y, swiglu=self.swiglu, split=split)
 
     def nbytes(self) -> int:
         n = self.words.numel() * 4 + self.scales.numel() * 2 + (self.zeros.numel() * 2 if self.zeros is not None else 0)

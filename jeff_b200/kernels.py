@@ -69,13 +69,16 @@ def lora_shrink(x: torch.Tensor, lora_a: torch.Tensor, adapters: torch.Tensor, r
 def int4_product(x: torch.Tensor, words: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor | None, group: int,
                  out_features: int, lora_a: torch.Tensor | None, lora_b: torch.Tensor | None,
                  adapters: torch.Tensor | None, row_len: int, mid: torch.Tensor | None = None,
-                 y: torch.Tensor | None = None, swiglu: bool = False, tmem_a: bool = False) -> torch.Tensor:
+                 y: torch.Tensor | None = None, swiglu: bool = False, tmem_a: bool = False,
+                 split: tuple[torch.Tensor, torch.Tensor] | None = None) -> torch.Tensor:
     """y (m, out) = bf16(x W^T + bf16(x A[a]^T) B[a]^T) for row a = adapters[t // row_len] of token t: the fused
     product of one group (module docstring); `words` in the kernel layout (int4_repack). lora_a (rows, R, k),
     lora_b (rows, columns, R) bf16, or None. swiglu: the group's columns are gate|up blocks of 64 and y (m, out / 2)
     receives bf16(bf16(silu(g)) u) (fast_path.silu_mul fused into the epilogue). tmem_a: the tensor-memory form of
     the product kernel (weights dequantised into tensor memory as the MMA's A operand; the same bits, measured
-    slower), for rows of a multiple of 128 tokens."""
+    slower), for rows of a multiple of 128 tokens. split (fp32 slices, int32 counters, the counters zero): the
+    split-K form (jb_int4_lora_product_split), which the library uses when the pass's tiles are fewer than the SMs;
+    the same result up to the order of the fp32 sums."""
     m, k = x.shape
     columns = words.shape[1]
     if words.shape[0] * 8 != k:
@@ -85,10 +88,17 @@ def int4_product(x: torch.Tensor, words: torch.Tensor, scales: torch.Tensor, zer
         y = torch.empty(m, out_features // 2 if swiglu else out_features, dtype=DT, device=x.device)
     if rank and mid is None:
         mid = torch.empty(m, rank, dtype=DT, device=x.device)
-    _lib.call("jb_int4_lora_product", ptr(x), m, k, ptr(words), ptr(scales), ptr(zeros), group, columns, out_features,
-              ptr(lora_a), ptr(lora_b), rank, 0 if lora_a is None else lora_a.shape[0], ptr(adapters), row_len,
-              ptr(mid) if rank else None, ptr(y), y.stride(0), (1 if swiglu else 0) | (2 if tmem_a else 0),
-              stream_ptr())
+    args = (ptr(x), m, k, ptr(words), ptr(scales), ptr(zeros), group, columns, out_features, ptr(lora_a), ptr(lora_b),
+            rank, 0 if lora_a is None else lora_a.shape[0], ptr(adapters), row_len, ptr(mid) if rank else None, ptr(y),
+            y.stride(0), (1 if swiglu else 0) | (2 if tmem_a else 0))
+    if split is None:
+        _lib.call("jb_int4_lora_product", *args, stream_ptr())
+    else:
+        parts, counters = split
+        _check(parts, "split partials", torch.float32)
+        _check(counters, "split counters", torch.int32)
+        _lib.call("jb_int4_lora_product_split", *args, ptr(parts), parts.numel(), ptr(counters), counters.numel(),
+                  stream_ptr())
     return y
 
 

@@ -44,8 +44,9 @@ def test_bad_arguments_are_refused_before_any_launch(lib: ctypes.CDLL) -> None:
     assert b"at most 256" in lib.jb_last_error()
     assert lib.jb_w4a16_lora(p, 40000, 1024, p, p, None, 64, 128, 128, p, p, 16, 3, p, 48, p, 128, 0, None) == -1
     assert b"at most 32768 tokens" in lib.jb_last_error()
-    # K not a multiple of 128 takes the 16-row shrink, whose blocks hold one adapter each
-    assert lib.jb_lora_shrink(p, 32, 64, p, 16, 1, p, 1, p, None) == -1
+    # pools of more than 256 rows take the mma.sync shrinks; with K not a multiple of 128 the 16-row one, whose blocks
+    # hold one adapter each
+    assert lib.jb_lora_shrink(p, 32, 64, p, 16, 300, p, 1, p, None) == -1
     assert b"multiples of 16" in lib.jb_last_error()
     with pytest.raises(_lib.ArgumentError, match="rank 20"):
         _lib.call("jb_lora_shrink", p, 32, 64, p, 20, 1, p, 32, p, None)

@@ -166,6 +166,75 @@ def test_int4_lora_product_within_its_error_bound(fmt: str, m: int, k: int, outs
     assert torch.equal(got, again)
 
 
+@pytest.mark.parametrize(("m", "k", "outs", "row_len"), [
+    (32, 1024, [6144, 2048, 16, 16], 32),         # the Gated DeltaNet projection of a batch-1 pass (32 tokens)
+    (32, 2048, [1024], 32),                       # out_proj: 8 tiles, K split 16 ways
+    (32, 3584, [1024], 32),                       # down_proj, K = 3584
+    (40, 1024, [4096, 512, 512], 8),              # ragged m, an adapter per 8 tokens
+    (128, 1024, [3584], 32),                      # four batch-1 rows
+    (512, 1024, [2048], 128),                     # two row tiles
+])
+def test_split_k_product_within_its_error_bound(m: int, k: int, outs: list[int], row_len: int) -> None:
+    """jb_int4_lora_product_split: every output within the product's forward-error bound (the slices' fp32 sums in
+    another order are covered by the same accumulation slack), the same bits on a second run, the tile counters
+    back at zero, and within the bound of the unsplit product's result too."""
+    g = torch.Generator().manual_seed(7 * m + k)
+    w = torch.randn(sum(outs), k, generator=g) * 0.02
+    packed, W = prod_int4.quantize_pack(w, "g128z")
+    rank = 16 * min(len(outs), 3)
+    pool_rows = 5
+    a_pool = (torch.randn(pool_rows, rank, k, generator=g) * 0.02).to(torch.bfloat16)
+    b_pool = torch.zeros(pool_rows, packed.columns, rank, dtype=torch.bfloat16)
+    b_pool[:, :sum(outs)] = (torch.randn(pool_rows, sum(outs), rank, generator=g) * 0.02).to(torch.bfloat16)
+    a_pool[0] = 0
+    b_pool[0] = 0
+    adapters = torch.randint(0, pool_rows, ((m + row_len - 1) // row_len,), generator=g, dtype=torch.int32)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    dev = packed.to("cuda")
+    dev = prod_int4.PackedInt4(kernels.int4_repack(dev.words), dev.scales, dev.zeros, dev.group, dev.out)
+    split = (torch.empty(4 * 2**20, dtype=torch.float32, device="cuda"),
+             torch.zeros(1024, dtype=torch.int32, device="cuda"))
+    args = (x.cuda(), dev.words, dev.scales, dev.zeros, packed.group, sum(outs), a_pool.cuda(), b_pool.cuda(),
+            adapters.cuda(), row_len)
+    got = kernels.int4_product(*args, split=split).cpu()
+    row_of = adapters.long().repeat_interleave(row_len)[:m]
+    exact, bound = exact_product(x.float(), W.float(), a_pool.float(), b_pool[:, :sum(outs)].float(), row_of)
+    err = (got.double() - exact).abs()
+    assert int((err > bound).sum()) == 0, f"worst at {(err / bound.clamp_min(1e-30)).max():.3g} x the bound"
+    assert torch.equal(kernels.int4_product(*args, split=split).cpu(), got)
+    assert not split[1].any()
+    plain = kernels.int4_product(*args).cpu()
+    assert int(((plain.double() - exact).abs() > bound).sum()) == 0
+
+
+def test_split_k_product_swiglu_epilogue() -> None:
+    """The SwiGLU epilogue after the slices are added: the gate/up group of a 32-token pass, as the unsplit
+    product's test bounds it (four bf16 steps, 5e-4 absolute near zero)."""
+    from jeff_b200.fast_path import swiglu_order
+
+    g = torch.Generator().manual_seed(78)
+    m, k, inter, row_len, rank, pool_rows = 32, 1024, 3584, 32, 32, 3
+    w = torch.randn(2 * inter, k, generator=g) * 0.02
+    packed, W = prod_int4.quantize_pack(w, "g128z")
+    order = swiglu_order(inter)
+    a_pool = (torch.randn(pool_rows, rank, k, generator=g) * 0.02).to(torch.bfloat16)
+    b_pool = (torch.randn(pool_rows, 2 * inter, rank, generator=g) * 0.02).to(torch.bfloat16)
+    adapters = torch.randint(0, pool_rows, (m // row_len,), generator=g, dtype=torch.int32)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    words = kernels.int4_repack(packed.words[:, order].contiguous().cuda())
+    split = (torch.empty(4 * 2**20, dtype=torch.float32, device="cuda"),
+             torch.zeros(1024, dtype=torch.int32, device="cuda"))
+    got = kernels.int4_product(x.cuda(), words, packed.scales[:, order].contiguous().cuda(),
+                               packed.zeros[:, order].contiguous().cuda(), packed.group, 2 * inter, a_pool.cuda(),
+                               b_pool[:, order].contiguous().cuda(), adapters.cuda(), row_len, swiglu=True,
+                               split=split).cpu().float()
+    row_of = adapters.long().repeat_interleave(row_len)
+    exact, _ = exact_product(x.float(), W.float(), a_pool.float(), b_pool.float(), row_of)
+    want = model_ref.silu_mul(bf(exact.float()))
+    torch.testing.assert_close(got, want, rtol=4 * BF16_STEP, atol=5e-4)
+    assert not split[1].any()
+
+
 @pytest.mark.parametrize("fmt", ["g128z", "g64"])
 def test_int4_lora_product_swiglu_epilogue(fmt: str) -> None:
     """The gate/up group with the SwiGLU epilogue (columns interleaved in blocks of 64): y = bf16(bf16(silu(g)) u)
