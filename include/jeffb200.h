@@ -85,14 +85,14 @@ int jb_int4_lora_product(const uint16_t* x, int m, int k, const int32_t* words, 
                          const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
                          uint16_t* mid, uint16_t* y, int ldy, int flags, void* stream);
 
-/* jb_int4_lora_product for passes too small to fill the GPU (the reference's small batch buckets, B * N down to 32
- * tokens): when the pass's 256 x 128 tiles are fewer than the SMs, each tile's K blocks are split into equal slices
- * (at least two blocks each, at most twice the SM count of work items), each slice a work item; the slices' fp32
- * sums go to `partials` (the caller's scratch, partial_floats floats: slices x columns rounded up to 128 x m rounded
- * up to 32), and the CTA whose slice arrives last adds them in slice order (deterministic) and stores y. `counters`
- * (counter_count int32, one per tile) must be zero before the first call; every call leaves them zero. Too little
- * scratch or too many tiles: the unsplit product. Same result as jb_int4_lora_product up to the order of the fp32
- * sums. Replaces int4_kernels.int4_product (int4_kernels.py:132-177) in the reference's batch-1 and small-batch
+/* jb_int4_lora_product for the smallest passes (the reference's batch-1 buckets: at most 64 tokens) of products with
+ * few tiles (at most a quarter as many 256 x 128 tiles as SMs: the 1024-wide out and down projections): each tile's K
+ * blocks are split into up to 4 equal slices of at least two blocks, each slice a work item; the slices' fp32 sums go
+ * to `partials` (the caller's scratch, partial_floats floats: slices x columns rounded up to 128 x m rounded up to
+ * 32), and the CTA whose slice arrives last adds them in slice order (deterministic) and stores y. `counters`
+ * (counter_count int32, one per tile) must be zero before the first call; every call leaves them zero. Other passes,
+ * too little scratch or too many tiles: the unsplit product. Same result as jb_int4_lora_product up to the order of
+ * the fp32 sums. Replaces int4_kernels.int4_product (int4_kernels.py:132-177) in the reference's batch-1 and small-batch
  * graphs. */
 int jb_int4_lora_product_split(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
                                const uint16_t* zeros, int group, int columns, int out, const uint16_t* lora_a,

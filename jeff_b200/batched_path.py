@@ -116,9 +116,9 @@ class BatchedPath:
         # outcomes identical to the oracle's from 1,022 to 1,023 (both remaining differences within 0.01 of the
         # 0.8 threshold)
         self.gdn_prefix_scan_kernel = "recurrent"
-        # split-K products for passes too small to fill the GPU (jb_int4_lora_product_split): measured slower than
-        # the unsplit product on batch-1 passes, so off
-        self.split_k = False
+        # products of passes too small to fill the GPU through jb_int4_lora_product_split (its LoRA shrink in K slices
+        # whenever its 128-token tiles are fewer than the SMs, the product itself only for few, long-K tiles)
+        self.split_k = True
         # attention: the tcgen05 kernel with the output gate fused (jb_paged_attention_gated); False runs the mma.sync
         # kernel and jb_gate_mul (the same result within the attention tolerance, tested)
         self.tc_attention = True

@@ -10,7 +10,7 @@
 // to bf16 and store the token's R values. Every adapter's terms are summed in K order by the tensor core whatever
 // other adapters share the tile, so a token's bits do not depend on the rest of the pass (packed rows give the bits
 // of padded ones). Waits are bounded (%globaltimer, 2 s): on expiry the CTA records JB_DEV_TIMEOUT | 60.. in the
-// device status word and returns.
+// device status word and returns. Passes of at most 128 tokens take dot_kernel (below) instead.
 
 namespace jb {
 namespace lsh {
@@ -51,7 +51,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 __global__ void __launch_bounds__(THREADS, 1)
     shrink_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_a, int M, int K,
                   int R, int pool_rows, const int* __restrict__ adapters, int row_len, __nv_bfloat16* __restrict__ mid,
-                  int* err, int splits, float* __restrict__ partials, int* __restrict__ counters) {
+                  int* err) {
   using L = Layout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -66,12 +66,8 @@ __global__ void __launch_bounds__(THREADS, 1)
   int* list = reinterpret_cast<int*>(smem + L::OFF_LIST);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // CTA = (token tile, K slice): with `splits` > 1 each slice sums K / splits of the inputs into fp32 partials
-  // ([slice][token][R]); the last slice of a tile to arrive adds them in slice order and stores mid
-  const int mt = blockIdx.x / splits, ks = blockIdx.x % splits;
-  const int m0 = mt * TM;
-  const int nkb = K / BK / splits;
-  const int kb0 = ks * nkb;
+  const int m0 = blockIdx.x * TM;
+  const int nkb = K / BK;
   const int per_pass = COLS / R;
 
   // this token's adapter (threads 0-127 are the tile's tokens); the tile's adapter set
@@ -124,10 +120,9 @@ __global__ void __launch_bounds__(THREADS, 1)
           const int s = it % STAGES;
           if (!mbar_wait(&empty[s], ((it / STAGES) & 1) ^ 1, abort_flag, err, 60)) break;
           mbar_arrive_expect_tx(&full[s], X_BYTES + dg * R * 128);
-          tma_load_2d(smem + L::OFF_X + s * X_BYTES, &tm_x, &full[s], (kb0 + kb) * BK, m0);
+          tma_load_2d(smem + L::OFF_X + s * X_BYTES, &tm_x, &full[s], kb * BK, m0);
           for (int j = 0; j < dg; ++j)
-            tma_load_3d(smem + L::OFF_B + s * B_BYTES + j * R * 128, &tm_a, &full[s], (kb0 + kb) * BK, 0,
-                        list[first + j]);
+            tma_load_3d(smem + L::OFF_B + s * B_BYTES + j * R * 128, &tm_a, &full[s], kb * BK, 0, list[first + j]);
         }
       }
     }
@@ -181,14 +176,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           uint32_t r[16];
           tmem_ld16(tmem + lane_bits + j * R + c0, r);
           tc_wait_ld();
-          if (mine && splits > 1) {
-            float4* dst = reinterpret_cast<float4*>(partials + ((size_t)ks * gridDim.x / splits * TM + (t - m0) +
-                                                                (size_t)mt * TM) * R + c0);
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-              dst[q] = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
-                                   __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
-          } else if (mine) {
+          if (mine) {
             uint4 v0, v1;
             v0.x = pack_bf2(__uint_as_float(r[0]), __uint_as_float(r[1]));
             v0.y = pack_bf2(__uint_as_float(r[2]), __uint_as_float(r[3]));
@@ -208,32 +196,6 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(tmem_empty);
     }
-    if (splits > 1) {
-      // the last slice of the tile adds the slices' partials of each token in slice order
-      volatile int* last_slice = reinterpret_cast<volatile int*>(smem + L::OFF_MISC + 12);
-      __threadfence();
-      named_barrier(1, 128);
-      if (tid == 0) *last_slice = atomicAdd(&counters[mt], 1) == splits - 1 ? 1 : 0;
-      named_barrier(1, 128);
-      if (*last_slice && t < M) {
-        __threadfence();
-        const size_t slice_stride = (size_t)gridDim.x / splits * TM * R;
-        const float* src = partials + (size_t)t * R;
-        for (int c0 = 0; c0 < R; c0 += 8) {
-          float4 a = __ldcg(reinterpret_cast<const float4*>(src + c0));
-          float4 b = __ldcg(reinterpret_cast<const float4*>(src + c0 + 4));
-          for (int k2 = 1; k2 < splits; ++k2) {
-            const float4 a2 = __ldcg(reinterpret_cast<const float4*>(src + k2 * slice_stride + c0));
-            const float4 b2 = __ldcg(reinterpret_cast<const float4*>(src + k2 * slice_stride + c0 + 4));
-            a.x += a2.x; a.y += a2.y; a.z += a2.z; a.w += a2.w;
-            b.x += b2.x; b.y += b2.y; b.z += b2.z; b.w += b2.w;
-          }
-          *reinterpret_cast<uint4*>(mid + (size_t)t * R + c0) =
-              make_uint4(pack_bf2(a.x, a.y), pack_bf2(a.z, a.w), pack_bf2(b.x, b.y), pack_bf2(b.z, b.w));
-        }
-      }
-      if (*last_slice && tid == 0) counters[mt] = 0;   // ready for the next launch
-    }
   }
   tc_fence_before();
   __syncthreads();
@@ -243,10 +205,53 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// Small passes (at most DOT_MAX_M tokens): one CTA per token, its x row staged in shared memory, each warp on ranks
+// w, w + 8, ...: lane-strided 16-byte loads of the adapter's A row, fp32 products summed per lane in K order, then a
+// fixed-order butterfly across the lanes; one bf16 rounding. Every (token, rank) is independent of the rest of the
+// pass, so packed rows still give the bits of padded ones. The tcgen05 kernel streams one 128-token tile's whole K
+// through a single CTA, which at these sizes is a latency chain of 16 to 56 K blocks.
+constexpr int DOT_MAX_M = 128;
+constexpr int DOT_THREADS = 256;
+
+__global__ void __launch_bounds__(DOT_THREADS) dot_kernel(const __nv_bfloat16* __restrict__ x, int K, int R,
+                                                          int pool_rows, const int* __restrict__ adapters,
+                                                          int row_len, const __nv_bfloat16* __restrict__ A,
+                                                          __nv_bfloat16* __restrict__ mid) {
+  extern __shared__ uint4 xrow[];   // K / 8 pieces of 8 inputs
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int a = adapters[t / row_len];
+  if (a < 0 || a >= pool_rows) a = 0;   // pool row 0: the zero adapter
+  const uint4* xs = reinterpret_cast<const uint4*>(x + (size_t)t * K);
+  for (int i = threadIdx.x; i < K / 8; i += DOT_THREADS) xrow[i] = xs[i];
+  __syncthreads();
+  for (int r = warp; r < R; r += DOT_THREADS / 32) {
+    const uint4* ar = reinterpret_cast<const uint4*>(A + ((size_t)a * R + r) * K);
+    float acc = 0.f;
+    for (int i = lane; i < K / 8; i += 32) {
+      const uint4 av = ar[i], xv = xrow[i];
+      acc = fmaf(bf_lo(av.x), bf_lo(xv.x), acc);
+      acc = fmaf(bf_hi(av.x), bf_hi(xv.x), acc);
+      acc = fmaf(bf_lo(av.y), bf_lo(xv.y), acc);
+      acc = fmaf(bf_hi(av.y), bf_hi(xv.y), acc);
+      acc = fmaf(bf_lo(av.z), bf_lo(xv.z), acc);
+      acc = fmaf(bf_hi(av.z), bf_hi(xv.z), acc);
+      acc = fmaf(bf_lo(av.w), bf_lo(xv.w), acc);
+      acc = fmaf(bf_hi(av.w), bf_hi(xv.w), acc);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+    if (lane == 0) mid[(size_t)t * R + r] = f2bf(acc);
+  }
+}
+
 // mid = bf16(x A[a]^T) for every token; JB_OK, or an error status (jb_last_error) when a map or the launch fails
 int launch(const __nv_bfloat16* x, int m, int k, const __nv_bfloat16* a, int rank, int pool_rows,
-           const int* adapters, int row_len, __nv_bfloat16* mid, cudaStream_t stream, int splits = 1,
-           float* partials = nullptr, int* counters = nullptr) {
+           const int* adapters, int row_len, __nv_bfloat16* mid, cudaStream_t stream) {
+  if (m <= DOT_MAX_M) {
+    dot_kernel<<<m, DOT_THREADS, (size_t)k * 2, stream>>>(x, k, rank, pool_rows, adapters, row_len, a, mid);
+    return check_launch("lora shrink dot_kernel");
+  }
   CUtensorMap tx, ta;
   int st = make_tmap_2d(&tx, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, k, m, (uint64_t)k * 2, BK, TM,
                         CU_TENSOR_MAP_SWIZZLE_128B);
@@ -258,8 +263,8 @@ int launch(const __nv_bfloat16* x, int m, int k, const __nv_bfloat16* a, int ran
   if (st) return st;
   cudaError_t e = cudaFuncSetAttribute(shrink_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout::ALLOC);
   if (e != cudaSuccess) return status_of(e, "lora shrink_kernel (tcgen05): shared memory attribute");
-  shrink_kernel<<<((m + TM - 1) / TM) * splits, THREADS, Layout::ALLOC, stream>>>(
-      tx, ta, m, k, rank, pool_rows, adapters, row_len, mid, device_status_word(), splits, partials, counters);
+  shrink_kernel<<<(m + TM - 1) / TM, THREADS, Layout::ALLOC, stream>>>(tx, ta, m, k, rank, pool_rows, adapters,
+                                                                       row_len, mid, device_status_word());
   return check_launch("lora shrink_kernel (tcgen05)");
 }
 

@@ -1101,34 +1101,20 @@ extern "C" int jb_int4_lora_product_split(const uint16_t* x, int m, int k, const
   const int kb = k / 64;
   if (rank > 0) {
     JB_REQUIRE(mid && lora_a && adapters, "jb_int4_lora_product_split: LoRA needs lora_a, adapters and mid");
-    // the shrink split the same way when its 128-token tiles are fewer than the SMs (the same scratch: the shrink
-    // is done with it, and its counters back at zero, before the product starts on the stream)
-    const int mt = (m + lsh::TM - 1) / lsh::TM;
-    int shrink_split = 1;
-    if (pool_rows <= lsh::MAX_POOL_ROWS && rank % 16 == 0 && rank >= 16 && rank <= 64 && row_len > 0 && mt < sms &&
-        mt <= counter_count &&
-        ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(lora_a) | reinterpret_cast<uintptr_t>(mid)) &
-         15) == 0) {
-      for (int s = kb / 2; s >= 2; --s)
-        if (kb % s == 0 && mt * s <= 2 * sms && (int64_t)s * mt * lsh::TM * rank <= partial_floats) {
-          shrink_split = s;
-          break;
-        }
-    }
-    int st = shrink_split > 1
-                 ? lsh::launch(reinterpret_cast<const __nv_bfloat16*>(x), m, k,
-                               reinterpret_cast<const __nv_bfloat16*>(lora_a), rank, pool_rows, adapters, row_len,
-                               reinterpret_cast<__nv_bfloat16*>(mid), (cudaStream_t)stream, shrink_split, partials,
-                               counters)
-                 : jb_lora_shrink(x, m, k, lora_a, rank, pool_rows, adapters, row_len, mid, stream);
+    // the shrink stays whole (slicing its K measured slower at 32 and 128 tokens)
+    int st = jb_lora_shrink(x, m, k, lora_a, rank, pool_rows, adapters, row_len, mid, stream);
     if (st) return st;
   }
   const int tiles = ((m + w4::BM - 1) / w4::BM) * ((columns + w4::BN - 1) / w4::BN);
   const int64_t ldp = ((m + 31) / 32) * 32;
   const int64_t per_slice = (int64_t)((columns + w4::BN - 1) / w4::BN) * w4::BN * ldp;
+  // measured on a B200: slicing pays for few, long-K tiles of the smallest passes (32 tokens: out_proj 8 tiles x 32
+  // K blocks 32 -> 25 us, down_proj 8 x 56 49 -> 31 us, both at 4 slices; more slices cost more) and costs where the
+  // tiles already spread over half the SMs (in_proj, 65 tiles: 22 -> 27 us) or at 128 tokens, so only passes of at
+  // most 64 tokens and at most a quarter as many tiles as SMs are sliced, into at most 4
   int split = 1;
-  if (!(flags & JB_PRODUCT_TMEM_A) && tiles < sms && tiles <= counter_count) {
-    for (int s = kb / 2; s >= 2; --s)
+  if (!(flags & JB_PRODUCT_TMEM_A) && m <= 64 && 4 * tiles <= sms && tiles <= counter_count) {
+    for (int s = kb / 2 < 4 ? kb / 2 : 4; s >= 2; --s)
       if (kb % s == 0 && tiles * s <= 2 * sms && s * per_slice <= partial_floats) {
         split = s;
         break;

@@ -208,12 +208,12 @@ def test_split_k_product_within_its_error_bound(m: int, k: int, outs: list[int],
 
 
 def test_split_k_product_swiglu_epilogue() -> None:
-    """The SwiGLU epilogue after the slices are added: the gate/up group of a 32-token pass, as the unsplit
-    product's test bounds it (four bf16 steps, 5e-4 absolute near zero)."""
+    """The SwiGLU epilogue after the slices are added: a gate/up group of 8 tiles (so the 32-token pass is sliced),
+    as the unsplit product's test bounds it (four bf16 steps, 5e-4 absolute near zero)."""
     from jeff_b200.fast_path import swiglu_order
 
     g = torch.Generator().manual_seed(78)
-    m, k, inter, row_len, rank, pool_rows = 32, 1024, 3584, 32, 32, 3
+    m, k, inter, row_len, rank, pool_rows = 32, 2048, 512, 32, 32, 3
     w = torch.randn(2 * inter, k, generator=g) * 0.02
     packed, W = prod_int4.quantize_pack(w, "g128z")
     order = swiglu_order(inter)
@@ -230,7 +230,9 @@ def test_split_k_product_swiglu_epilogue() -> None:
                                split=split).cpu().float()
     row_of = adapters.long().repeat_interleave(row_len)
     exact, _ = exact_product(x.float(), W.float(), a_pool.float(), b_pool.float(), row_of)
-    want = model_ref.silu_mul(bf(exact.float()))
+    gu = bf(exact.float())
+    gate, up = gu[:, :inter], gu[:, inter:]
+    want = bf(bf(gate * torch.sigmoid(gate)) * up)      # silu_mul (fast_path.py:141-156) of this narrower group
     torch.testing.assert_close(got, want, rtol=4 * BF16_STEP, atol=5e-4)
     assert not split[1].any()
 
@@ -309,16 +311,17 @@ def test_tensor_memory_product_gives_the_bits_of_the_shared_memory_form(fmt: str
 
 
 @pytest.mark.parametrize(("m", "k", "rank", "row_len"), [
-    (256, 1024, 48, 64),      # staged kernel (32-row blocks of one adapter)
-    (512, 3584, 16, 128),     # staged, K = 3584
-    (208, 2048, 64, 64),      # staged, m not a multiple of the 32-row block
-    (384, 1024, 32, 128),     # staged
-    (256, 1024, 48, 32),      # staged, rows of 32 tokens
-    (96, 1024, 32, 16),       # 16-row kernel: rows of 16 tokens
-    (96, 960, 16, 32),        # 16-row kernel: K not a multiple of 128
-    (200, 1024, 16, 1),       # staged, one adapter id per token: blocks of several adapters
-    (240, 2048, 32, 48),      # staged, rows of 48 tokens: blocks that span two rows
-    (100, 1024, 64, 7),       # staged, rows of 7 tokens, m not a multiple of the block
+    (256, 1024, 48, 64),      # tcgen05 kernel: 128-token tiles of two adapters
+    (512, 3584, 16, 128),     # tcgen05, K = 3584
+    (208, 2048, 64, 64),      # tcgen05, m not a multiple of the 128-token tile
+    (384, 1024, 32, 128),     # tcgen05
+    (256, 1024, 48, 32),      # tcgen05, rows of 32 tokens: four adapters in a tile (two passes at rank 48)
+    (96, 1024, 32, 16),       # small pass (dot kernel): rows of 16 tokens
+    (96, 960, 16, 32),        # small pass: K not a multiple of 128
+    (200, 1024, 16, 1),       # tcgen05, one adapter id per token: every adapter of the pool in a tile
+    (240, 2048, 32, 48),      # tcgen05, rows of 48 tokens: tiles that span rows
+    (100, 1024, 64, 7),       # small pass, rows of 7 tokens
+    (32, 3584, 48, 32),       # small pass: a batch-1 row of the down projection's K
 ])
 def test_lora_shrink_matches_the_oracle(m: int, k: int, rank: int, row_len: int) -> None:
     """mid = bf16(x A[a]^T) per row's adapter: within one bf16 step of the float32 product (summation order), and the
