@@ -33,6 +33,9 @@ OPTIONS = 32
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reps", type=int, default=50)
+    ap.add_argument("--profile", action="store_true",
+                    help="run one batch-1 decision (N = 32) inside cudaProfilerStart/Stop (for ncu "
+                         "--profile-from-start off) and exit")
     args = ap.parse_args()
     torch.cuda.set_device(0)
     model = synthetic.make_model(synthetic.ModelSpec())
@@ -43,7 +46,7 @@ def main() -> None:
     texts = {f"prefix {a}": torch.randint(0, 151936, (PREFIX_TOKENS,), generator=g).tolist() for a in range(ADAPTERS)}
     path = BatchedPath(fast, tokenize=lambda t: texts[t])
     shapes = [(1, 32), (1, 64), (1, 128), (1, 256)] + [(b, n) for n in (32, 64, 128) for b in (4, 16, 64)]
-    path.record(shapes)
+    path.record(shapes[:1] if args.profile else shapes)
     slots, _ = path.ensure_prefixes([(rows_of[a], f"prefix {a}") for a in range(ADAPTERS)], max_tokens=8192)
 
     def rows(b: int, n: int, seed: int) -> list[tuple[int, int, Row]]:
@@ -53,6 +56,16 @@ def main() -> None:
                 for i in range(b)]
 
     try:
+        if args.profile:
+            call = rows(1, 32, 1)
+            for _ in range(3):
+                path.decide(call)
+            torch.cuda.synchronize()
+            torch.cuda.profiler.start()
+            path.decide(call)
+            torch.cuda.synchronize()
+            torch.cuda.profiler.stop()
+            return
         for n in (32, 64, 128, 256):
             calls = [rows(1, n, 100 * n + r) for r in range(args.reps + 5)]
             for c in calls[:5]:
