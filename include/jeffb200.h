@@ -219,6 +219,17 @@ int jb_paged_attention_gated(const uint16_t* q, const void* pool, int64_t pool_p
                              const int32_t* tables, int table_stride, int kv_entry, int attn_layer, int attn_layers,
                              const int32_t* pos, const uint16_t* kn, const uint16_t* vn, const uint16_t* pr, int ldpr,
                              uint16_t* y, int ldy, int b, int n, void* stream);
+/* jb_paged_attention_gated with each row's key walk split over several CTAs when the unsplit walk's CTAs (b x 2 x
+ * n / 32) leave SMs idle (batch-1 and small passes): enough slices to cover the SMs, at most 16, as many as `scratch`
+ * (scratch_floats fp32: per slice b n x 8 x 258) holds; each slice keeps its unnormalised O, running max and row
+ * sum, and a combine kernel adds the slices in order (deterministic) before the same bf16 roundings and gate. The
+ * same result up to the order of the fp32 sums. Replaces batched_kernels.paged_attention's split into 1/2/4/8/16
+ * programs plus its combine (batched_kernels.py:370-486), chosen per graph there (batched_path.py:101-104). */
+int jb_paged_attention_gated_split(const uint16_t* q, const void* pool, int64_t pool_pages, int64_t page_bytes,
+                                   const int32_t* tables, int table_stride, int kv_entry, int attn_layer,
+                                   int attn_layers, const int32_t* pos, const uint16_t* kn, const uint16_t* vn,
+                                   const uint16_t* pr, int ldpr, uint16_t* y, int ldy, int b, int n, float* scratch,
+                                   int64_t scratch_floats, void* stream);
 /* The prefix pass's page scatter: each row's new keys/values (tokens below ceil(real[r] / 32) * 32) into its
  * pages out_tables[r][kv_entry + j / 32] of attention layer attn_layer. Replaces pool.kv.index_copy_
  * (batched_path.py:345-349). */

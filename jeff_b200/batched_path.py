@@ -116,8 +116,9 @@ class BatchedPath:
         # outcomes identical to the oracle's from 1,022 to 1,023 (both remaining differences within 0.01 of the
         # 0.8 threshold)
         self.gdn_prefix_scan_kernel = "recurrent"
-        # products of passes too small to fill the GPU through jb_int4_lora_product_split (its LoRA shrink in K slices
-        # whenever its 128-token tiles are fewer than the SMs, the product itself only for few, long-K tiles)
+        # passes too small to fill the GPU: products through jb_int4_lora_product_split (K slices for the smallest
+        # passes' few-tile products) and the attention through jb_paged_attention_gated_split (the key walk in slices),
+        # both on the workspace's split scratch
         self.split_k = True
         # attention: the tcgen05 kernel with the output gate fused (jb_paged_attention_gated); False runs the mma.sync
         # kernel and jb_gate_mul (the same result within the attention tolerance, tested)
@@ -219,7 +220,8 @@ class BatchedPath:
                     if li == len(f.layers) - 1:
                         return None   # the last layer: only its keys and values are kept
                 if self.tc_attention:
-                    y = kernels.paged_attention_gated(aq, pool, attn_tables, ai, pos, kn, vn, n, pr, out=ws.y[:t])
+                    y = kernels.paged_attention_gated(aq, pool, attn_tables, ai, pos, kn, vn, n, pr, out=ws.y[:t],
+                                                      scratch=ws.split[0] if self.split_k else None)
                 else:
                     ao = kernels.paged_attention(aq, pool, attn_tables, ai, pos, kn, vn, n, out=ws.ao[:t])
                     y = kernels.gate_mul(ao, pr, out=ws.y[:t])

@@ -60,6 +60,10 @@ struct Params {
   int n;
   float scale_log2;
   int* err;
+  // split walk: gridDim.z slices of each row's key tiles; slice z writes its unnormalised O, running max and row sum
+  // to part (O [z][token][query head][256], then m, l [z][token][query head][2], fp32) and combine_kernel finishes
+  int splits;
+  float* part;
 };
 
 // 2^x by the hardware's approximate base-2 exponential (PTX ex2.approx.ftz.f32), as the reference's Triton
@@ -108,7 +112,11 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int P = p.pos[row];
   const int pre_tiles = (P + BKN - 1) / BKN;
   const int q_hi = (qb + 1) * BQ;                      // new keys this block may see: [0, q_hi)
-  const int tiles = pre_tiles + (q_hi + BKN - 1) / BKN;
+  const int all_tiles = pre_tiles + (q_hi + BKN - 1) / BKN;
+  // this CTA's key tiles [j0, j0 + tiles) of the row's, an even slice when the walk is split; barrier phases count
+  // the CTA's own tiles (jj), key positions the row's (j)
+  const int j0 = (int)((long long)all_tiles * blockIdx.z / p.splits);
+  const int tiles = (int)((long long)all_tiles * (blockIdx.z + 1) / p.splits) - j0;
   const int tok0 = row * p.n + qb * BQ;                 // the block's first token in the pass
 
   if (threadIdx.x == 0) {
@@ -166,15 +174,15 @@ __global__ void __launch_bounds__(THREADS, 1)
           for (int c = 0; c < 4; ++c) tma_load_3d(dst + c * (BKN * 128) + half * (PAGE * 128), map, bar, 64 * c, g, r0);
         }
       };
-      for (int j = 0; j < tiles; ++j) {
-        const int s = j % STAGES;
-        const uint32_t ph = ((j / STAGES) & 1) ^ 1;
+      for (int jj = 0; jj < tiles; ++jj) {
+        const int s = jj % STAGES;
+        const uint32_t ph = ((jj / STAGES) & 1) ^ 1;
         if (!mbar_wait(&k_free[s], ph, abort_flag, p.err, 21)) break;
         mbar_arrive_expect_tx(&k_full[s], KV_BYTES);
-        load(j, false, smem + OFF_K + s * KV_BYTES, &k_full[s]);
+        load(j0 + jj, false, smem + OFF_K + s * KV_BYTES, &k_full[s]);
         if (!mbar_wait(&v_free[s], ph, abort_flag, p.err, 31)) break;
         mbar_arrive_expect_tx(&v_full[s], KV_BYTES);
-        load(j, true, smem + OFF_V + s * KV_BYTES, &v_full[s]);
+        load(j0 + jj, true, smem + OFF_V + s * KV_BYTES, &v_full[s]);
       }
     }
   } else if (warp == 1) {
@@ -236,12 +244,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     float* xmax = reinterpret_cast<float*>(smem + OFF_RED);          // [2 tiles][2 halves][128 rows]
     float m = -1e30f, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < tiles && ok; ++j) {
-      ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1, abort_flag, p.err, 26);
+    for (int jj = 0; jj < tiles && ok; ++jj) {
+      const int j = j0 + jj;
+      ok = mbar_wait(&s_full[jj & 1], (jj >> 1) & 1, abort_flag, p.err, 26);
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
       tc_fence_after();
       uint32_t sv[32];   // this half's 32 scores of the row
-      tmem_ld32(tmem + lane_bits + TM_S + 64 * (j & 1) + 32 * half, sv);
+      tmem_ld32(tmem + lane_bits + TM_S + 64 * (jj & 1) + 32 * half, sv);
       tc_wait_ld();
       const bool prefix = j < pre_tiles;
       const int key0 = (prefix ? j * BKN : (j - pre_tiles) * BKN) + 32 * half;
@@ -251,18 +260,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       for (int c = 0; c < 32; ++c)
         if (c < limit) mine = fmaxf(mine, __uint_as_float(sv[c]));
       mine = mine > -1e30f ? mine * p.scale_log2 : -1e30f;
-      xmax[((j & 1) * 2 + half) * 128 + r] = mine;
+      xmax[((jj & 1) * 2 + half) * 128 + r] = mine;
       __syncwarp();
-      if (lane == 0) mbar_arrive(&xchg[j & 1]);
-      ok = mbar_wait(&xchg[j & 1], (j >> 1) & 1, abort_flag, p.err, 32);   // both halves' maxima of tile j are in
+      if (lane == 0) mbar_arrive(&xchg[jj & 1]);
+      ok = mbar_wait(&xchg[jj & 1], (jj >> 1) & 1, abort_flag, p.err, 32);   // both halves' maxima of tile j are in
       if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
-      const float mx = fmaxf(m, fmaxf(mine, xmax[((j & 1) * 2 + (half ^ 1)) * 128 + r]));
+      const float mx = fmaxf(m, fmaxf(mine, xmax[((jj & 1) * 2 + (half ^ 1)) * 128 + r]));
       // P buffer j % 2 is free once the value product of tile j - 2 is done (o_done); O may be rescaled only after
       // the value product of tile j - 1
-      if (j >= 1) {
+      if (jj >= 1) {
         const bool rescale = mx > m + 8.0f;
         // warp-uniform: a warp that rescales any of its rows touches all 32 rows' O, so it waits for tile j - 1
-        const int wait_for = __any_sync(0xffffffffu, rescale) ? j - 1 : j - 2;
+        const int wait_for = __any_sync(0xffffffffu, rescale) ? jj - 1 : jj - 2;
         if (wait_for >= 0) {
           ok = mbar_wait(&o_done[wait_for & 1], (wait_for >> 1) & 1, abort_flag, p.err, 27);
           if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
@@ -289,7 +298,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       // P = bf16(exp2(s - m)) into the swizzled K-major P tile (row r: 64 keys = 128 B; this half's 4 chunks of 16
       // B), this half's row sum unrounded
-      uint8_t* pt = smem + OFF_P + (j & 1) * P_BYTES;
+      uint8_t* pt = smem + OFF_P + (jj & 1) * P_BYTES;
       float rs = 0.f;
 #pragma unroll
       for (int c8 = 0; c8 < 4; ++c8) {
@@ -307,8 +316,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int tile_key0 = prefix ? j * BKN : 0;
       if (prefix && P - tile_key0 < BKN) {
         // stale page contents past the prefix: zero those V rows (P is 0 there, but 0 x NaN is NaN)
-        const int s = j % STAGES;
-        ok = mbar_wait(&v_full[s], (j / STAGES) & 1, abort_flag, p.err, 28);
+        const int s = jj % STAGES;
+        ok = mbar_wait(&v_full[s], (jj / STAGES) & 1, abort_flag, p.err, 28);
         if (!__all_sync(0xffffffffu, ok)) { ok = false; break; }
         uint8_t* vt = smem + OFF_V + s * KV_BYTES;
         const int first = P - tile_key0 > 0 ? P - tile_key0 : 0;
@@ -320,12 +329,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_ready[j & 1]);
+      if (lane == 0) mbar_arrive(&p_ready[jj & 1]);
     }
     // ---------------- epilogue: O / l -> bf16, times bf16(sigmoid(gate)) -> y (this half's 128 columns). The two
     // halves' sums meet in the exchange buffer of the parity the last tile did not use (its last reader, tile
     // tiles - 2, finished before the last tile's barrier).
-    float* xsum = xmax + (tiles & 1) * 2 * 128;
+    float* xsum = xmax + (tiles & 1) * 2 * 128;   // (tiles: this CTA's own count)
     xsum[half * 128 + r] = l;
     __syncwarp();
     if (lane == 0) mbar_arrive(xsum_bar);
@@ -335,7 +344,35 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int jl = tiles - 1;
       ok = mbar_wait(&o_done[jl & 1], (jl >> 1) & 1, abort_flag, p.err, 29);
     }
-    if (__all_sync(0xffffffffu, ok)) {
+    if (__all_sync(0xffffffffu, ok) && p.splits > 1) {
+      // a slice of a split walk: unnormalised O (relative to this slice's max m), m and l for combine_kernel
+      tc_fence_after();
+      const int t = tok0 + i;
+      const int qh = 4 * g + h;
+      const size_t tq = ((size_t)blockIdx.z * gridDim.x / NKV * p.n + t) * NQ + qh;   // (slice, token, head)
+      float* orow = p.part + tq * HD + 128 * half;
+#pragma unroll 1
+      for (int cc = 0; cc < HD / 64; ++cc) {
+        uint32_t ov[32];
+        if (tiles > 0) {
+          tmem_ld32(tmem + lane_bits + TM_O + 128 * half + 32 * cc, ov);
+          tc_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] = 0u;
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          *reinterpret_cast<float4*>(orow + 32 * cc + 4 * q4) =
+              make_float4(__uint_as_float(ov[4 * q4]), __uint_as_float(ov[4 * q4 + 1]),
+                          __uint_as_float(ov[4 * q4 + 2]), __uint_as_float(ov[4 * q4 + 3]));
+      }
+      if (half == 0) {
+        float* ml = p.part + (size_t)p.splits * (gridDim.x / NKV) * p.n * NQ * HD + tq * 2;
+        ml[0] = m;
+        ml[1] = l;
+      }
+    } else if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       const int t = tok0 + i;
@@ -371,6 +408,29 @@ __global__ void __launch_bounds__(THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+}
+
+// The slices of a split walk, per (token, query head): M = the slices' largest max, O = sum_z 2^(m_z - M) O_z,
+// L = sum_z 2^(m_z - M) l_z in slice order (deterministic); then the unsplit epilogue: bf16(O / L) times
+// bf16(sigmoid(gate)), rounded. One block of 256 threads (one per value column) per (token, query head).
+__global__ void __launch_bounds__(HD) combine_kernel(const float* __restrict__ part, int splits, int tokens,
+                                                     const __nv_bfloat16* __restrict__ pr, int ldpr,
+                                                     __nv_bfloat16* __restrict__ y, int ldy) {
+  const int t = blockIdx.x / NQ, qh = blockIdx.x % NQ, d = threadIdx.x;
+  const size_t rows = (size_t)tokens * NQ;
+  const float* ml = part + (size_t)splits * rows * HD;
+  float M = -1e30f;
+  for (int z = 0; z < splits; ++z) M = fmaxf(M, ml[(z * rows + blockIdx.x) * 2]);
+  float o = 0.f, L = 0.f;
+  for (int z = 0; z < splits; ++z) {
+    const float mz = ml[(z * rows + blockIdx.x) * 2], lz = ml[(z * rows + blockIdx.x) * 2 + 1];
+    const float w = lz > 0.f ? ex2(mz - M) : 0.f;
+    o += w * part[(z * rows + blockIdx.x) * HD + d];
+    L += w * lz;
+  }
+  const float inv = L > 0.f ? 1.0f / L : 0.f;
+  const float g = bf2f(pr[(size_t)t * ldpr + qh * 2 * HD + HD + d]);
+  y[(size_t)t * ldy + qh * HD + d] = f2bf(round_bf(o * inv) * round_bf(1.0f / (1.0f + expf(-g))));
 }
 
 // A 3-D bf16 tensor map {HD dims, heads, rows} with head stride `head_bytes` and row stride `row_bytes`, box
@@ -409,12 +469,13 @@ inline int make_map(CUtensorMap* map, const void* base, uint64_t heads, uint64_t
 }  // namespace atc
 }  // namespace jb
 
-extern "C" int jb_paged_attention_gated(const uint16_t* q, const void* pool, int64_t pool_pages, int64_t page_bytes,
-                                        const int32_t* tables, int table_stride, int kv_entry, int attn_layer,
-                                        int attn_layers, const int32_t* pos, const uint16_t* kn, const uint16_t* vn,
-                                        const uint16_t* pr, int ldpr, uint16_t* y, int ldy, int b, int n,
-                                        void* stream) {
-  using namespace jb;
+namespace jb {
+namespace atc {
+// the gated attention with the key walk in `splits` slices (1: the whole walk in one CTA, no scratch)
+static int gated_impl(const uint16_t* q, const void* pool, int64_t pool_pages, int64_t page_bytes,
+                      const int32_t* tables, int table_stride, int kv_entry, int attn_layer, int attn_layers,
+                      const int32_t* pos, const uint16_t* kn, const uint16_t* vn, const uint16_t* pr, int ldpr,
+                      uint16_t* y, int ldy, int b, int n, int splits, float* part, void* stream) {
   JB_REQUIRE(q && pool && tables && pos && kn && vn && pr && y, "jb_paged_attention_gated: null pointer");
   JB_REQUIRE(b > 0 && n > 0 && n % atc::BQ == 0, "jb_paged_attention_gated: b %d, n %d (a multiple of 32)", b, n);
   JB_REQUIRE(pool_pages > 0 && attn_layer >= 0 && attn_layer < attn_layers &&
@@ -437,11 +498,53 @@ extern "C" int jb_paged_attention_gated(const uint16_t* q, const void* pool, int
   if ((st = atc::make_map(&tvn, vn, atc::NKV, t, atc::HD * 2, (uint64_t)atc::NKV * atc::HD * 2))) return st;
   atc::Params p{tables, table_stride, kv_entry, attn_layer, attn_layers, pos,
                 reinterpret_cast<const __nv_bfloat16*>(pr), ldpr, reinterpret_cast<__nv_bfloat16*>(y), ldy, n,
-                (1.0f / 16.0f) * 1.4426950408889634f, device_status_word()};
+                (1.0f / 16.0f) * 1.4426950408889634f, device_status_word(), splits, part};
   if ((st = status_of(cudaFuncSetAttribute(atc::attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            atc::ALLOC), "attention: shared memory attribute")))
     return st;
-  dim3 grid(b * atc::NKV, n / atc::BQ);
+  dim3 grid(b * atc::NKV, n / atc::BQ, splits);
   atc::attention_kernel<<<grid, atc::THREADS, atc::ALLOC, (cudaStream_t)stream>>>(tq, tpool, tkn, tvn, p);
-  return check_launch("attention_kernel (tcgen05)");
+  if ((st = check_launch("attention_kernel (tcgen05)"))) return st;
+  if (splits > 1) {
+    atc::combine_kernel<<<(unsigned)(t * atc::NQ), atc::HD, 0, (cudaStream_t)stream>>>(
+        part, splits, (int)t, reinterpret_cast<const __nv_bfloat16*>(pr), ldpr, reinterpret_cast<__nv_bfloat16*>(y),
+        ldy);
+    return check_launch("attention combine_kernel");
+  }
+  return JB_OK;
+}
+}  // namespace atc
+}  // namespace jb
+
+extern "C" int jb_paged_attention_gated(const uint16_t* q, const void* pool, int64_t pool_pages, int64_t page_bytes,
+                                        const int32_t* tables, int table_stride, int kv_entry, int attn_layer,
+                                        int attn_layers, const int32_t* pos, const uint16_t* kn, const uint16_t* vn,
+                                        const uint16_t* pr, int ldpr, uint16_t* y, int ldy, int b, int n,
+                                        void* stream) {
+  return jb::atc::gated_impl(q, pool, pool_pages, page_bytes, tables, table_stride, kv_entry, attn_layer,
+                             attn_layers, pos, kn, vn, pr, ldpr, y, ldy, b, n, 1, nullptr, stream);
+}
+
+extern "C" int jb_paged_attention_gated_split(const uint16_t* q, const void* pool, int64_t pool_pages,
+                                              int64_t page_bytes, const int32_t* tables, int table_stride,
+                                              int kv_entry, int attn_layer, int attn_layers, const int32_t* pos,
+                                              const uint16_t* kn, const uint16_t* vn, const uint16_t* pr, int ldpr,
+                                              uint16_t* y, int ldy, int b, int n, float* scratch,
+                                              int64_t scratch_floats, void* stream) {
+  using namespace jb;
+  JB_REQUIRE(scratch && (reinterpret_cast<uintptr_t>(scratch) & 15) == 0,
+             "jb_paged_attention_gated_split: scratch must be a 16-byte aligned pointer");
+  JB_REQUIRE(b > 0 && n > 0 && n % atc::BQ == 0, "jb_paged_attention_gated_split: b %d, n %d (a multiple of 32)",
+             b, n);
+  // slices only when the CTAs of the unsplit walk leave SMs idle: enough slices to cover the SMs (at most 16), as
+  // many as the scratch holds (per slice, O and m, l of every token and query head)
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int ctas = b * atc::NKV * (n / atc::BQ);
+  const int64_t per_slice = (int64_t)b * n * atc::NQ * (atc::HD + 2);
+  int splits = ctas >= sms ? 1 : (sms + ctas - 1) / ctas;
+  if (splits > 16) splits = 16;
+  while (splits > 1 && splits * per_slice > scratch_floats) --splits;
+  return atc::gated_impl(q, pool, pool_pages, page_bytes, tables, table_stride, kv_entry, attn_layer, attn_layers,
+                         pos, kn, vn, pr, ldpr, y, ldy, b, n, splits, scratch, stream);
 }

@@ -299,10 +299,11 @@ def paged_attention(q: torch.Tensor, pool, tables: torch.Tensor, attn_layer: int
 
 def paged_attention_gated(q: torch.Tensor, pool, tables: torch.Tensor, attn_layer: int, pos: torch.Tensor,
                           kn: torch.Tensor, vn: torch.Tensor, n: int, pr: torch.Tensor,
-                          out: torch.Tensor | None = None) -> torch.Tensor:
+                          out: torch.Tensor | None = None, scratch: torch.Tensor | None = None) -> torch.Tensor:
     """Paged prefix-KV attention on tcgen05 with the output gate fused (paged_attention then gate_mul in one launch):
     y (t, 2048) bf16 = bf16(bf16(attention) * bf16(sigmoid(gate))), the gate half of each head's q_proj output in
-    pr."""
+    pr. scratch (fp32): the split walk's (jb_paged_attention_gated_split), which passes too small to fill the GPU
+    spread over more CTAs."""
     t = q.shape[0]
     b = _pass_rows(t, n)
     width = pool.fixed_pages + pool.max_kv_pages
@@ -313,9 +314,14 @@ def paged_attention_gated(q: torch.Tensor, pool, tables: torch.Tensor, attn_laye
         if not x.is_contiguous():
             raise ValueError(f"paged_attention_gated: {name} must be contiguous")
     y = out if out is not None else torch.empty(t, C.NQ * C.HD, dtype=DT, device=q.device)
-    _lib.call("jb_paged_attention_gated", ptr(q), ptr(pool.data), pool.pages, pool.shapes.page_bytes, ptr(tables),
-              tables.stride(0), pool.fixed_pages, attn_layer, pool.shapes.attn_layers, ptr(pos), ptr(kn), ptr(vn),
-              ptr(pr), pr.stride(0), ptr(y), y.stride(0), b, n, stream_ptr())
+    args = (ptr(q), ptr(pool.data), pool.pages, pool.shapes.page_bytes, ptr(tables), tables.stride(0),
+            pool.fixed_pages, attn_layer, pool.shapes.attn_layers, ptr(pos), ptr(kn), ptr(vn), ptr(pr), pr.stride(0),
+            ptr(y), y.stride(0), b, n)
+    if scratch is None:
+        _lib.call("jb_paged_attention_gated", *args, stream_ptr())
+    else:
+        _check(scratch, "attention scratch", torch.float32)
+        _lib.call("jb_paged_attention_gated_split", *args, ptr(scratch), scratch.numel(), stream_ptr())
     return y
 
 

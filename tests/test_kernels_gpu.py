@@ -778,22 +778,29 @@ def gated_oracle(q, kp, vp, kn, vn, pr_rows):
     return model_ref.gate_mul(o, gate)
 
 
+@pytest.mark.parametrize("split", [False, True])
 @pytest.mark.parametrize("b", BATCHES)
 @pytest.mark.parametrize("n", [32, 64, 128])
-def test_gated_attention_on_tensor_memory_matches_the_oracle(pool_fixture, b: int, n: int) -> None:
+def test_gated_attention_on_tensor_memory_matches_the_oracle(pool_fixture, b: int, n: int, split: bool) -> None:
     """The tcgen05 kernel (S and O in tensor memory, K / V pages by TMA, the gate fused): prefix keys read in place
     from pages that hold NaN past each prefix's end (those V rows must be zeroed, not multiplied by zero), prefixes of
     0 to 1,000 tokens (partial pages, a partial last tile of 64 keys), the new keys causally, attention layers 0 and 5.
     Against the oracle's attention and gate multiply within ATTN_RTOL (plus one bf16 step for the second rounding) and
     ATTN_ATOL; and against the mma.sync kernel + jb_gate_mul within twice that (each is within it of the exact
-    result)."""
+    result). split: the key walk in slices with a combine (jb_paged_attention_gated_split: up to 16 slices at one
+    row, so short prefixes leave slices with no keys), the same bounds, and the same bits on a second call."""
     pool, slots, states = pool_fixture
     ss = pass_slots(slots, b, seed=b * 13 + n)
     tables, pos = tables_for(pool, ss)
     q, kn, vn, pr = attention_inputs(b * n, seed=b * 3 + n)
+    scratch = torch.empty(4 * 2**20, dtype=torch.float32, device="cuda") if split else None
     for layer in (0, 5):
         got = kernels.paged_attention_gated(q.cuda(), pool, tables, layer, pos, kn.cuda(), vn.cuda(), n,
-                                            pr.cuda()).cpu()
+                                            pr.cuda(), scratch=scratch).cpu()
+        if split:
+            again = kernels.paged_attention_gated(q.cuda(), pool, tables, layer, pos, kn.cuda(), vn.cuda(), n,
+                                                  pr.cuda(), scratch=scratch).cpu()
+            assert torch.equal(got, again)
         assert not got.isnan().any(), "the kernel let a NaN past a prefix's last token into the sums"
         old = kernels.gate_mul(kernels.paged_attention(q.cuda(), pool, tables, layer, pos, kn.cuda(), vn.cuda(), n),
                                pr.cuda()).cpu()
