@@ -25,6 +25,8 @@ extern "C" {
 #define JB_ECUDA (-2)    /* a CUDA runtime error */
 #define JB_ETIMEOUT (-3) /* a device-side bounded wait gave up (see jb_device_status) */
 #define JB_DEV_TIMEOUT 0x10000 /* device status word: a bounded wait gave up; low bits say where */
+#define JB_DEV_LAUNCH 0x20000  /* device status word: a kernel found itself launched in another shape than its host
+                                  code set (a thread-block cluster of the wrong size); low bits say which kernel */
 #define JB_PRODUCT_SWIGLU 1    /* product flag: columns are gate|up blocks of 64; y = bf16(bf16(silu(g)) u) */
 #define JB_PRODUCT_TMEM_A 2    /* product flag: the tensor-memory form (weights dequantised straight into tensor
                                   memory as the MMA's A operand) where it applies; the same bits, measured slower */
@@ -76,6 +78,20 @@ int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* words, const u
                   int rank, int pool_rows, const int32_t* adapters, int row_len, uint16_t* y, int ldy, int flags,
                   void* stream);
 
+/* jb_w4a16_lora for passes of at most 64 tokens in at most two LoRA rows (row_len tokens each), streaming the
+ * weights: one CTA per (128-column tile, K slice), every K block of its slice loaded at once (TMA) and dequantised
+ * into tcgen05 MMAs with the tokens as N (m rounded up to 16); the slices of a tile are one thread-block cluster and
+ * add their fp32 sums in slice order over distributed shared memory (deterministic), each storing its share of the
+ * tokens. split: K slices per tile, 1, 2, 4 or 8, dividing k / 64 and leaving each slice a multiple of 4 of the
+ * m-rounded-up-to-16 tokens and a slice that fits in shared memory; 0 chooses the most whose grid still fits on the
+ * SMs at once. LoRA (mid given): each row's expand, its adapter's B rows by TMA. Same arguments and flags as
+ * jb_w4a16_lora otherwise. Replaces int4_kernels.int4_product (int4_kernels.py:132-177) in the reference's batch-1
+ * and small-batch graphs, which pick their product kernel per recorded pass (product_choice.py:1-13, 69-84). */
+int jb_w4a16_lora_small(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
+                        const uint16_t* zeros, int group, int columns, int out, const uint16_t* mid,
+                        const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
+                        uint16_t* y, int ldy, int flags, int split, void* stream);
+
 /* jb_lora_shrink then jb_w4a16_lora, with the caller's scratch `mid` (at least m * rank bf16). flags: 0, or
  * JB_PRODUCT_SWIGLU for a gate/up group whose columns are interleaved in blocks of 64 (gate 64, up 64, ...): then y
  * (m, out / 2) = bf16(bf16(silu(g)) u) of the rounded products, the reference's silu_mul (fast_path.py:141-156)
@@ -85,15 +101,14 @@ int jb_int4_lora_product(const uint16_t* x, int m, int k, const int32_t* words, 
                          const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
                          uint16_t* mid, uint16_t* y, int ldy, int flags, void* stream);
 
-/* jb_int4_lora_product for the smallest passes (the reference's batch-1 buckets: at most 64 tokens) of products with
- * few tiles (at most a quarter as many 256 x 128 tiles as SMs: the 1024-wide out and down projections): each tile's K
- * blocks are split into up to 4 equal slices of at least two blocks, each slice a work item; the slices' fp32 sums go
- * to `partials` (the caller's scratch, partial_floats floats: slices x columns rounded up to 128 x m rounded up to
- * 32), and the CTA whose slice arrives last adds them in slice order (deterministic) and stores y. `counters`
- * (counter_count int32, one per tile) must be zero before the first call; every call leaves them zero. Other passes,
- * too little scratch or too many tiles: the unsplit product. Same result as jb_int4_lora_product up to the order of
- * the fp32 sums. Replaces int4_kernels.int4_product (int4_kernels.py:132-177) in the reference's batch-1 and small-batch
- * graphs. */
+/* jb_int4_lora_product for small passes, with the caller's split scratch. Passes of at most 64 tokens in at most two
+ * LoRA rows (the reference's batch-1 and two-row buckets) run jb_w4a16_lora_small with its own choice of K slices.
+ * Other passes of at most 64 tokens with few tiles (at most a quarter as many 256 x 128 tiles as SMs) take the
+ * persistent kernel with its K split into up to 4 slices: `partials` (partial_floats floats) holds the slices' fp32
+ * sums, `counters` (counter_count int32, one per tile) must be zero before the first call and are left zero. Too
+ * little scratch: fewer slices. Same result as jb_int4_lora_product up to the order of the fp32 sums (slices added
+ * in slice order: deterministic). Replaces int4_kernels.int4_product (int4_kernels.py:132-177) in the reference's
+ * batch-1 and small-batch graphs. */
 int jb_int4_lora_product_split(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
                                const uint16_t* zeros, int group, int columns, int out, const uint16_t* lora_a,
                                const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,

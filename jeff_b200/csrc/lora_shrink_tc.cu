@@ -205,51 +205,52 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
-// Small passes (at most DOT_MAX_M tokens): one CTA per token, its x row staged in shared memory, each warp on ranks
-// w, w + 8, ...: lane-strided 16-byte loads of the adapter's A row, fp32 products summed per lane in K order, then a
-// fixed-order butterfly across the lanes; one bf16 rounding. Every (token, rank) is independent of the rest of the
-// pass, so packed rows still give the bits of padded ones. The tcgen05 kernel streams one 128-token tile's whole K
-// through a single CTA, which at these sizes is a latency chain of 16 to 56 K blocks.
+// Small passes (at most DOT_MAX_M tokens): one warp per (token, rank) dot, DOT_ROWS ranks of one token per CTA
+// (grid: tokens x ceil(R / DOT_ROWS)), so a 32-token pass of rank 48 runs 384 CTAs instead of a latency chain on a
+// few SMs. Each lane reads its 16-byte pieces i = lane, lane + 32, ... of the x row and of the adapter's A row (both
+// from L2, several pieces in flight), sums its fp32 products in K order, then a fixed-order butterfly across the
+// lanes; one bf16 rounding. Every (token, rank) is independent of the rest of the pass, so packed rows still give the
+// bits of padded ones. The tcgen05 kernel streams one 128-token tile's whole K through a single CTA, which at these
+// sizes is a latency chain of 16 to 56 K blocks.
 constexpr int DOT_MAX_M = 128;
-constexpr int DOT_THREADS = 256;
+constexpr int DOT_THREADS = 128;
+constexpr int DOT_ROWS = DOT_THREADS / 32;   // ranks per CTA: one per warp
 
 __global__ void __launch_bounds__(DOT_THREADS) dot_kernel(const __nv_bfloat16* __restrict__ x, int K, int R,
                                                           int pool_rows, const int* __restrict__ adapters,
                                                           int row_len, const __nv_bfloat16* __restrict__ A,
                                                           __nv_bfloat16* __restrict__ mid) {
-  extern __shared__ uint4 xrow[];   // K / 8 pieces of 8 inputs
   const int t = blockIdx.x;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.y * DOT_ROWS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r >= R) return;   // whole warps
   int a = adapters[t / row_len];
   if (a < 0 || a >= pool_rows) a = 0;   // pool row 0: the zero adapter
   const uint4* xs = reinterpret_cast<const uint4*>(x + (size_t)t * K);
-  for (int i = threadIdx.x; i < K / 8; i += DOT_THREADS) xrow[i] = xs[i];
-  __syncthreads();
-  for (int r = warp; r < R; r += DOT_THREADS / 32) {
-    const uint4* ar = reinterpret_cast<const uint4*>(A + ((size_t)a * R + r) * K);
-    float acc = 0.f;
-    for (int i = lane; i < K / 8; i += 32) {
-      const uint4 av = ar[i], xv = xrow[i];
-      acc = fmaf(bf_lo(av.x), bf_lo(xv.x), acc);
-      acc = fmaf(bf_hi(av.x), bf_hi(xv.x), acc);
-      acc = fmaf(bf_lo(av.y), bf_lo(xv.y), acc);
-      acc = fmaf(bf_hi(av.y), bf_hi(xv.y), acc);
-      acc = fmaf(bf_lo(av.z), bf_lo(xv.z), acc);
-      acc = fmaf(bf_hi(av.z), bf_hi(xv.z), acc);
-      acc = fmaf(bf_lo(av.w), bf_lo(xv.w), acc);
-      acc = fmaf(bf_hi(av.w), bf_hi(xv.w), acc);
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-    if (lane == 0) mid[(size_t)t * R + r] = f2bf(acc);
+  const uint4* ar = reinterpret_cast<const uint4*>(A + ((size_t)a * R + r) * K);
+  float acc = 0.f;
+#pragma unroll 4
+  for (int i = lane; i < K / 8; i += 32) {
+    const uint4 av = __ldg(ar + i), xv = __ldg(xs + i);
+    acc = fmaf(bf_lo(av.x), bf_lo(xv.x), acc);
+    acc = fmaf(bf_hi(av.x), bf_hi(xv.x), acc);
+    acc = fmaf(bf_lo(av.y), bf_lo(xv.y), acc);
+    acc = fmaf(bf_hi(av.y), bf_hi(xv.y), acc);
+    acc = fmaf(bf_lo(av.z), bf_lo(xv.z), acc);
+    acc = fmaf(bf_hi(av.z), bf_hi(xv.z), acc);
+    acc = fmaf(bf_lo(av.w), bf_lo(xv.w), acc);
+    acc = fmaf(bf_hi(av.w), bf_hi(xv.w), acc);
   }
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) mid[(size_t)t * R + r] = f2bf(acc);
 }
 
 // mid = bf16(x A[a]^T) for every token; JB_OK, or an error status (jb_last_error) when a map or the launch fails
 int launch(const __nv_bfloat16* x, int m, int k, const __nv_bfloat16* a, int rank, int pool_rows,
            const int* adapters, int row_len, __nv_bfloat16* mid, cudaStream_t stream) {
   if (m <= DOT_MAX_M) {
-    dot_kernel<<<m, DOT_THREADS, (size_t)k * 2, stream>>>(x, k, rank, pool_rows, adapters, row_len, a, mid);
+    dot_kernel<<<dim3(m, (rank + DOT_ROWS - 1) / DOT_ROWS), DOT_THREADS, 0, stream>>>(x, k, rank, pool_rows,
+                                                                                     adapters, row_len, a, mid);
     return check_launch("lora shrink dot_kernel");
   }
   CUtensorMap tx, ta;

@@ -877,6 +877,7 @@ __global__ void int4_repack_kernel(const int32_t* __restrict__ in, int32_t* __re
 }  // namespace jb
 
 #include "w4a16_tmem.cu"
+#include "w4a16_small.cu"
 
 using namespace jb;
 
@@ -940,6 +941,7 @@ extern "C" int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* l
 namespace jb {
 namespace w4 {
 // jb_w4a16_lora with split K: k_split slices per tile (1: none), partials and counters the caller's scratch
+// k_split < 0: the small-pass kernel (w4a16_small.cu) with -k_split - 1 slices (0: its own choice)
 static int w4a16_lora_impl(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
                            const uint16_t* zeros, int group, int columns, int out, const uint16_t* mid,
                            const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters, int row_len,
@@ -977,6 +979,14 @@ static int w4a16_lora_impl(const uint16_t* x, int m, int k, const int32_t* words
       JB_REQUIRE((m + row_len - 1) / row_len <= w4::Layout::MAX_ROWS, "jb_w4a16_lora: more than %d rows",
                  w4::Layout::MAX_ROWS);
     }
+  }
+  if (k_split < 0) {
+    if (lora)
+      JB_REQUIRE((reinterpret_cast<uintptr_t>(mid) & 15) == 0 && (reinterpret_cast<uintptr_t>(lora_b) & 15) == 0,
+                 "jb_w4a16_lora: mid and lora_b must be 16-byte aligned");
+    if (zeros) JB_REQUIRE((reinterpret_cast<uintptr_t>(zeros) & 15) == 0, "jb_w4a16_lora: zeros alignment");
+    return w4s::launch(x, m, k, words, scales, zeros, group, columns, out, lora ? mid : nullptr, lora_b, rank,
+                       pool_rows, adapters, row_len, y, ldy, swiglu, -k_split - 1, (cudaStream_t)stream);
   }
   // JB_PRODUCT_TMEM_A: the tensor-memory form (w4a16_tmem.cu), for calls whose LoRA rows are whole 128-token halves
   // (or one row for the whole pass); the same bits. Measured on a B200 at the Gated DeltaNet in_proj shape it takes
@@ -1047,12 +1057,28 @@ extern "C" int jb_w4a16_lora(const uint16_t* x, int m, int k, const int32_t* wor
                              adapters, row_len, y, ldy, flags, 1, nullptr, nullptr, stream);
 }
 
+extern "C" int jb_w4a16_lora_small(const uint16_t* x, int m, int k, const int32_t* words, const uint16_t* scales,
+                                   const uint16_t* zeros, int group, int columns, int out, const uint16_t* mid,
+                                   const uint16_t* lora_b, int rank, int pool_rows, const int32_t* adapters,
+                                   int row_len, uint16_t* y, int ldy, int flags, int split, void* stream) {
+  JB_REQUIRE(split >= 0 && split <= w4s::MAX_SPLIT, "jb_w4a16_lora_small: split %d (0 to %d)", split,
+             w4s::MAX_SPLIT);
+  return w4::w4a16_lora_impl(x, m, k, words, scales, zeros, group, columns, out, mid, lora_b, rank, pool_rows,
+                             adapters, row_len, y, ldy, flags, -split - 1, nullptr, nullptr, stream);
+}
+
 #ifdef JB_TRACE
 // Measurement builds only (python -m jeff_b200.build --trace, libjeffb200_trace.so): copies the shared-memory
 // product kernel's stage trace, 16 x 256 clock64() stamps of CTA 0's hand-offs in its last launch, to `out`. Not
 // part of the product library or its header.
 extern "C" int jb_prod_trace_read(uint64_t* out) {
   return status_of(cudaMemcpyFromSymbol(out, w4::g_prod_trace, sizeof(w4::g_prod_trace)), "jb_prod_trace_read");
+}
+extern "C" int jb_small_trace_read(uint64_t* out) {
+  return status_of(cudaMemcpyFromSymbol(out, w4s::g_small_trace, sizeof(w4s::g_small_trace)), "jb_small_trace_read");
+}
+extern "C" int jb_small_span_read(uint64_t* out) {
+  return status_of(cudaMemcpyFromSymbol(out, w4s::g_small_span, sizeof(w4s::g_small_span)), "jb_small_span_read");
 }
 extern "C" int jb_stage_trace_read(uint64_t* out) {
   JB_REQUIRE(out, "jb_stage_trace_read: null pointer");
@@ -1105,6 +1131,10 @@ extern "C" int jb_int4_lora_product_split(const uint16_t* x, int m, int k, const
     int st = jb_lora_shrink(x, m, k, lora_a, rank, pool_rows, adapters, row_len, mid, stream);
     if (st) return st;
   }
+  // passes of at most 64 tokens in at most two LoRA rows: the weight-streaming kernel, its K slices one cluster
+  if (!(flags & JB_PRODUCT_TMEM_A) && w4s::plan(m, k, columns, rank, row_len, group) > 0)
+    return w4::w4a16_lora_impl(x, m, k, words, scales, zeros, group, columns, out, rank > 0 ? mid : nullptr, lora_b,
+                               rank, pool_rows, adapters, row_len, y, ldy, flags, -1, partials, counters, stream);
   const int tiles = ((m + w4::BM - 1) / w4::BM) * ((columns + w4::BN - 1) / w4::BN);
   const int64_t ldp = ((m + 31) / 32) * 32;
   const int64_t per_slice = (int64_t)((columns + w4::BN - 1) / w4::BN) * w4::BN * ldp;

@@ -102,6 +102,24 @@ def int4_product(x: torch.Tensor, words: torch.Tensor, scales: torch.Tensor, zer
     return y
 
 
+def w4a16_small(x: torch.Tensor, words: torch.Tensor, scales: torch.Tensor, zeros: torch.Tensor | None, group: int,
+                out_features: int, mid: torch.Tensor | None, lora_b: torch.Tensor | None,
+                adapters: torch.Tensor | None, row_len: int, split: int = 0, swiglu: bool = False,
+                y: torch.Tensor | None = None) -> torch.Tensor:
+    """The weight-streaming product for passes of at most 64 tokens in at most two LoRA rows (jb_w4a16_lora_small):
+    y = bf16(x W^T + mid B[a]^T), mid the LoRA first factor (m, R) already computed (or None). split: K slices per
+    128-column tile, one thread-block cluster (0: the library's choice)."""
+    m, k = x.shape
+    columns = words.shape[1]
+    rank = 0 if mid is None else mid.shape[1]
+    if y is None:
+        y = torch.empty(m, out_features // 2 if swiglu else out_features, dtype=DT, device=x.device)
+    _lib.call("jb_w4a16_lora_small", ptr(x), m, k, ptr(words), ptr(scales), ptr(zeros), group, columns, out_features,
+              ptr(mid), ptr(lora_b), rank, 0 if lora_b is None else lora_b.shape[0], ptr(adapters), row_len, ptr(y),
+              y.stride(0), 1 if swiglu else 0, split, stream_ptr())
+    return y
+
+
 # ---------------------------------------------------------------- norms and activations
 
 

@@ -346,8 +346,11 @@ def test_cfg4_graph_replays_are_deterministic_and_well_formed(cfg4) -> None:
 
 
 def test_decide_groups_rows_by_bucket_and_keeps_order(cfg4) -> None:
-    """Rows of mixed lengths (buckets 32, 64, 128) through decide(): each row's probabilities equal those of the same
-    row alone in a B = 1 pass of its bucket."""
+    """Rows of mixed lengths (buckets 32, 64, 128) through decide(): each row keeps its place, and its probabilities
+    agree with those of the same row alone in a B = 1 pass of its bucket by the reference's rule for a row in a pass
+    against the row alone (runtime/python/tests/test_batched_path_cuda.py:38-47, 222-243): the same top option and no
+    probability more than 0.03 apart. The two passes are not bit for bit the same because a small pass takes other
+    kernel forms (the products' K split over CTAs, the attention's key walk split), which round differently."""
     model, adapters, fast, path, rows, part, slots = cfg4
     mixed = []
     for j, (adapter, slot, row) in enumerate(part[:6]):
@@ -357,5 +360,9 @@ def test_decide_groups_rows_by_bucket_and_keeps_order(cfg4) -> None:
     assert timing["passes"] == 3 and sorted(set(timing["bucket"])) == [32, 64, 128]
     for j, item in enumerate(mixed):
         alone, _, _ = path.decide([item])
-        np.testing.assert_allclose(together[j], alone[0], rtol=0, atol=2e-3)
+        c = item[2].count
+        top2 = np.sort(alone[0][:c])[-2:]
+        if top2[1] - top2[0] > 1e-2:   # the reference's rows exclude near ties from the top-option check
+            assert int(np.argmax(together[j][:c])) == int(np.argmax(alone[0][:c]))
+        np.testing.assert_allclose(together[j], alone[0], rtol=0, atol=3e-2)
         assert tokens[j] == 512 + len(item[2].new_ids)

@@ -207,6 +207,79 @@ def test_split_k_product_within_its_error_bound(m: int, k: int, outs: list[int],
     assert int(((plain.double() - exact).abs() > bound).sum()) == 0
 
 
+@pytest.mark.parametrize("m,k,outs,row_len,rank,split,fmt", [
+    (1, 1024, [3584], 1, 16, 0, "g128z"),                     # one token, the library's choice of slices
+    (16, 1024, [6144, 2048, 16, 16], 16, 48, 4, "g128z"),     # in_proj-like group, ragged last tile
+    (32, 2048, [1024], 32, 16, 8, "g128z"),                   # out_proj, eight slices
+    (32, 3584, [1024], 16, 32, 8, "g64"),                     # down_proj, two rows of two adapters, symmetric g64
+    (16, 256, [1024], 16, 16, 1, "g128z"),                    # one slice: the persistent kernel's sums and order
+    (64, 1024, [4096, 512, 512], 32, 16, 2, "g128z"),         # two rows of 32 tokens, two slices
+    (40, 1024, [2048], 8, 0, 0, "g128z"),                     # no LoRA (ragged 48-token box)
+])
+def test_small_product_within_its_error_bound(m: int, k: int, outs: list[int], row_len: int, rank: int, split: int,
+                                              fmt: str) -> None:
+    """jb_w4a16_lora_small against the float64 product: every output within the product's forward-error bound and
+    the same bits on a second run; with one slice, the same bits as the persistent kernel (jb_w4a16_lora: the same
+    sums in the same K order)."""
+    g = torch.Generator().manual_seed(11 * m + k + split)
+    w = torch.randn(sum(outs), k, generator=g) * 0.02
+    packed, W = prod_int4.quantize_pack(w, fmt)
+    pool_rows = 5
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    adapters = torch.randint(0, pool_rows, ((m + row_len - 1) // row_len,), generator=g, dtype=torch.int32)
+    if rank:
+        a_pool = (torch.randn(pool_rows, rank, k, generator=g) * 0.02).to(torch.bfloat16)
+        b_pool = torch.zeros(pool_rows, packed.columns, rank, dtype=torch.bfloat16)
+        b_pool[:, :sum(outs)] = (torch.randn(pool_rows, sum(outs), rank, generator=g) * 0.02).to(torch.bfloat16)
+        a_pool[0] = 0
+        b_pool[0] = 0
+        row_of = adapters.long().repeat_interleave(row_len)[:m]
+        mid = torch.einsum("tk,trk->tr", x.float(), a_pool.float()[row_of]).to(torch.bfloat16)
+    dev = packed.to("cuda")
+    words = kernels.int4_repack(dev.words)
+    zeros = dev.zeros if fmt == "g128z" else None
+    args = (x.cuda(), words, dev.scales, zeros, packed.group, sum(outs), mid.cuda() if rank else None,
+            b_pool.cuda() if rank else None, adapters.cuda(), row_len)
+    got = kernels.w4a16_small(*args, split=split).cpu()
+    exact = x.double() @ W.double().T
+    mag = x.double().abs() @ W.double().abs().T
+    if rank:
+        b_rows = b_pool.double()[row_of][:, :sum(outs)]
+        exact += torch.einsum("tr,tnr->tn", mid.double(), b_rows)
+        mag += torch.einsum("tr,tnr->tn", mid.double().abs(), b_rows.abs())
+    # one bf16 rounding of the result, the fp32 accumulation slack over k + rank terms (mid is an exact input here)
+    _, e = torch.frexp(exact.abs())
+    step = torch.where(exact == 0, torch.zeros_like(exact), torch.ldexp(torch.ones_like(exact), e - 8))
+    bound = step + (k + rank) * 2.0 ** -23 * mag
+    err = (got.double() - exact).abs()
+    assert int((err > bound).sum()) == 0, f"worst at {(err / bound.clamp_min(1e-30)).max():.3g} x the bound"
+    assert torch.equal(kernels.w4a16_small(*args, split=split).cpu(), got)
+    if split == 1:
+        plain = torch.empty(m, sum(outs), dtype=torch.bfloat16, device="cuda")
+        kernels._lib.call("jb_w4a16_lora", kernels.ptr(args[0]), m, k, kernels.ptr(words), kernels.ptr(dev.scales),
+                          kernels.ptr(zeros), packed.group, words.shape[1], sum(outs), kernels.ptr(args[6]),
+                          kernels.ptr(args[7]), rank, pool_rows, kernels.ptr(args[8]), row_len, kernels.ptr(plain),
+                          plain.stride(0), 0, kernels.stream_ptr())
+        assert torch.equal(plain.cpu(), got)
+
+
+def test_small_product_refuses_what_it_cannot_hold() -> None:
+    """Three LoRA rows, a split that leaves a slice a ragged token count, and a slice too big for shared memory are
+    refused before any launch (the split entry sends such passes to the persistent kernel instead)."""
+    x = torch.zeros(48, 3584, dtype=torch.bfloat16, device="cuda")
+    words = torch.zeros(3584 // 8, 1024, dtype=torch.int32, device="cuda")
+    scales = torch.ones(3584 // 128, 1024, dtype=torch.bfloat16, device="cuda")
+    mid = torch.zeros(48, 16, dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros(2, 1024, 16, dtype=torch.bfloat16, device="cuda")
+    adp = torch.zeros(3, dtype=torch.int32, device="cuda")
+    with pytest.raises(kernels._lib.ArgumentError, match="LoRA rows"):
+        kernels.w4a16_small(x, words, scales, None, 128, 1024, mid, b, adp, 16)
+    with pytest.raises(kernels._lib.ArgumentError, match="multiple of 4"):
+        kernels.w4a16_small(x, words, scales, None, 128, 1024, None, None, None, 48, split=8)
+    with pytest.raises(kernels._lib.ArgumentError, match="shared memory"):
+        kernels.w4a16_small(x, words, scales, None, 128, 1024, None, None, None, 48, split=1)
+
+
 def test_split_k_product_swiglu_epilogue() -> None:
     """The SwiGLU epilogue after the slices are added: a gate/up group of 8 tiles (so the 32-token pass is sliced),
     as the unsplit product's test bounds it (four bf16 steps, 5e-4 absolute near zero)."""
