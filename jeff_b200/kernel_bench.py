@@ -6,7 +6,10 @@ configurations 1 and 3 (bench.py reports the whole decision pass; this reports s
 cfg1: one int4 W4A16 + LoRA product: M 64 tokens, K 1024, N 3584, one rank-16 adapter, int4 group 128 with bf16
   scales and zeros. Algorithmic bytes per call 2,686,976 (words 1,835,008 + scales 57,344 + zeros 57,344 + x 131,072
   + y 458,752 + A 32,768 + B 114,688): HBM-bound. Timed as a CUDA graph of 256 calls cycling through enough distinct
-  weight copies to exceed twice the 126 MB L2, so each call streams its weights from HBM.
+  weight copies to exceed twice the 126 MB L2, so each call streams its weights from HBM; once through the persistent
+  kernel (jb_int4_lora_product) and once through the small-pass route the batched path takes (the split entry: the
+  warp-per-dot LoRA shrink and the weight-streaming kernel with its K slices one cluster).
+small: the products of one batch-1 decision (32 new tokens, one row), each shape through both routes the same way.
 cfg2: the projection sweep over one decoder layer (q 1024->2048, k and v 1024->512, o 2048->1024, gate and up
   1024->3584, down 3584->1024, q with its gate 1024->4096): 64 requests of 32 to 128 tokens packed into M = 4096 rows
   with one adapter id per token, 8 rank-16 adapters, int4 group 128 with bf16 scales and zeros. Per projection
@@ -101,9 +104,86 @@ def cfg1(reps: int) -> dict:
     with torch.cuda.graph(graph):
         body()
     ms = timed(graph.replay, reps) / calls
+    scratch = (torch.empty(4 * 2**20, dtype=torch.float32, device="cuda"),
+               torch.zeros(1024, dtype=torch.int32, device="cuda"))
+
+    def body_small() -> None:
+        for i in range(calls):
+            j = i % copies
+            kernels.int4_product(x, words[j], scales[j], zeros[j], packed.group, n, a_pool, b_pool, adapters, m,
+                                 mid=mid, y=y, split=scratch)
+
+    body_small()
+    torch.cuda.synchronize()
+    graph_small = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph_small):
+        body_small()
+    small_ms = timed(graph_small.replay, reps) / calls
     algo = 1_835_008 + 57_344 + 57_344 + 131_072 + 458_752 + 32_768 + 114_688
-    return {"kernel": "w4a16_lora (lora_shrink + w4a16_lora_kernel)", "config": "cfg1 M64 K1024 N3584 rank16 g128z",
-            "ms": ms, "bytes": algo, "weight_copies": copies}
+    config = "cfg1 M64 K1024 N3584 rank16 g128z"
+    return [{"kernel": "w4a16_lora (lora_shrink + w4a16_lora_kernel)", "config": config, "ms": ms, "bytes": algo,
+             "weight_copies": copies},
+            {"kernel": "small-pass route (lsh::dot_kernel + w4s::small_kernel, K slices one cluster)",
+             "config": config, "ms": small_ms, "bytes": algo, "weight_copies": copies}]
+
+
+def small(reps: int) -> list[dict]:
+    """The products of one batch-1 decision (32 new tokens of one row, one adapter, configuration 4's int4 g128 + zero
+    base), each shape as the batched path runs it at 32 tokens: the LoRA first factor (dot kernel) and the
+    weight-streaming small-pass product through jb_int4_lora_product_split, beside the persistent kernel
+    (jb_int4_lora_product) on the same call. Weights cycled past twice the L2 between calls; algorithmic bytes: the
+    int4 words, scales and zeros, x, y, the adapter's A and B rows and mid."""
+    m, rank_of = 32, {"in_proj": 48, "qkv": 48, "out_proj": 16, "o_proj": 16, "gate_up": 32, "down": 16}
+    shapes = [("in_proj", 1024, C.GDN_PROJ), ("qkv", 1024, C.ATTN_PROJ), ("out_proj", 2048, 1024),
+              ("o_proj", 2048, 1024), ("gate_up", 1024, 2 * C.INTER), ("down", C.INTER, 1024)]
+    lines = []
+    for name, k, n in shapes:
+        rank = rank_of[name]
+        packed, _ = int4.quantize_pack(synthetic.normal(1, f"small/{name}", (n, k), 0.02), "g128z")
+        per_copy = packed.words.numel() * 4 + packed.scales.numel() * 2 + packed.zeros.numel() * 2
+        copies = math.ceil(2 * L2_BYTES / per_copy)
+        dev = packed.to("cuda")
+        words = [kernels.int4_repack(dev.words.clone()) for _ in range(copies)]
+        scales = [dev.scales.clone() for _ in range(copies)]
+        zeros = [dev.zeros.clone() for _ in range(copies)]
+        a_pool = (0.02 * torch.randn(2, rank, k, device="cuda")).to(torch.bfloat16)
+        b_pool = (0.01 * torch.randn(2, packed.columns, rank, device="cuda")).to(torch.bfloat16)
+        adapters = torch.ones(1, dtype=torch.int32, device="cuda")
+        x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+        y = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
+        mid = torch.empty(m, rank, dtype=torch.bfloat16, device="cuda")
+        scratch = (torch.empty(4 * 2**20, dtype=torch.float32, device="cuda"),
+                   torch.zeros(1024, dtype=torch.int32, device="cuda"))
+        calls = 64
+        res = {}
+        for route, split in (("persistent", None), ("small", scratch)):
+            def body() -> None:
+                for i in range(calls):
+                    j = i % copies
+                    kernels.int4_product(x, words[j], scales[j], zeros[j], packed.group, n, a_pool, b_pool, adapters,
+                                         m, mid=mid, y=y, split=split)
+
+            body()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                body()
+            res[route] = timed(graph.replay, reps) / calls
+            del graph
+        algo = per_copy + m * k * 2 + m * n * 2 + rank * (k + n) * 2 + m * rank * 2
+        lines.append({"kernel": "small-pass route (lsh::dot_kernel + w4s::small_kernel)",
+                      "config": f"batch-1 {name} M{m} K{k} N{n} rank{rank} g128z", "ms": res["small"],
+                      "persistent_ms": res["persistent"], "bytes": algo, "weight_copies": copies})
+        del words, scales, zeros
+        torch.cuda.empty_cache()
+    lines.append({"kernel": "batch-1 products of a Gated DeltaNet layer (in_proj, out_proj, gate_up, down)",
+                  "config": "batch-1 M32", "ms": sum(x["ms"] for x in lines if x["config"].split()[1] in
+                                                      ("in_proj", "out_proj", "gate_up", "down")),
+                  "persistent_ms": sum(x["persistent_ms"] for x in lines if x["config"].split()[1] in
+                                       ("in_proj", "out_proj", "gate_up", "down")),
+                  "bytes": sum(x["bytes"] for x in lines if x["config"].split()[1] in
+                               ("in_proj", "out_proj", "gate_up", "down"))})
+    return lines
 
 
 def cfg2(reps: int) -> list[dict]:
@@ -247,15 +327,15 @@ def cfg4_attention(reps: int) -> list[dict]:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reps", type=int, default=20)
-    ap.add_argument("--only", choices=["cfg1", "cfg2", "cfg3", "attention"], default=None)
+    ap.add_argument("--only", choices=["cfg1", "cfg2", "cfg3", "attention", "small"], default=None)
     args = ap.parse_args()
     if not torch.cuda.is_available():
         raise SystemExit("kernel_bench needs a CUDA GPU")
     torch.cuda.set_device(0)
     peak, source = hbm_peak()
     tpeak, tsource = tensor_peak()
-    runs = {"cfg1": lambda: [cfg1(args.reps)], "cfg2": lambda: cfg2(args.reps), "cfg3": lambda: cfg3(args.reps),
-            "attention": lambda: cfg4_attention(args.reps)}
+    runs = {"cfg1": lambda: cfg1(args.reps), "cfg2": lambda: cfg2(args.reps), "cfg3": lambda: cfg3(args.reps),
+            "attention": lambda: cfg4_attention(args.reps), "small": lambda: small(args.reps)}
     chosen = [args.only] if args.only else list(runs)
     for line in [x for name in chosen for x in runs[name]()]:
         gbs = line["bytes"] / (line["ms"] / 1e3) / 1e9
