@@ -30,6 +30,7 @@ __global__ void __launch_bounds__(384) prep_kernel(const __nv_bfloat16* __restri
                                                    const float* __restrict__ inv_freq, const int* __restrict__ pos,
                                                    __nv_bfloat16* __restrict__ q, __nv_bfloat16* __restrict__ kn,
                                                    __nv_bfloat16* __restrict__ vn) {
+  pdl_begin();
   const int t = blockIdx.x;
   const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = t / n;
@@ -121,6 +122,7 @@ __global__ void __launch_bounds__(256, 1) paged_attention_kernel(
     const int* __restrict__ tables, int table_stride, int kv_entry, int attn_layer, int attn_layers,
     const int* __restrict__ pos, const __nv_bfloat16* __restrict__ kn, const __nv_bfloat16* __restrict__ vn,
     __nv_bfloat16* __restrict__ out, int n, float scale_log2) {
+  pdl_begin();
   extern __shared__ __align__(16) uint8_t sm[];
   // [buffer 0: K tile, V tile][buffer 1: K tile, V tile]
   const int row = blockIdx.x / NKV, g = blockIdx.x % NKV;
@@ -312,6 +314,7 @@ __global__ void __launch_bounds__(256, 1) paged_attention_kernel(
 __global__ void kv_scatter_kernel(const __nv_bfloat16* __restrict__ kn, const __nv_bfloat16* __restrict__ vn, int b,
                                   int n, const int* __restrict__ real, uint8_t* __restrict__ pool, int64_t page_bytes,
                                   const int* __restrict__ out_tables, int table_stride, int kv_entry, int attn_layer) {
+  pdl_begin();
   constexpr int CH = NKV * HD * 2 / 16;   // 16-byte chunks per token per K or V
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)b * n * 2 * CH) return;
@@ -340,7 +343,7 @@ extern "C" int jb_attn_prep_rows(const uint16_t* pr, int ldpr, int t, int n, con
   JB_REQUIRE(t > 0 && n > 0 && t % n == 0, "jb_attn_prep_rows: a pass of %d tokens in rows of %d", t, n);
   JB_REQUIRE(ldpr >= attn::NQ * 2 * attn::HD + 2 * attn::NKV * attn::HD && ldpr % 8 == 0, "jb_attn_prep_rows: ldpr %d",
              ldpr);
-  attn::prep_kernel<<<t, 384, 0, (cudaStream_t)stream>>>(
+  launch_pdl(attn::prep_kernel, t, 384, 0, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(pr), ldpr, n, q_w1, k_w1, inv_freq, pos,
       reinterpret_cast<__nv_bfloat16*>(q), reinterpret_cast<__nv_bfloat16*>(kn), reinterpret_cast<__nv_bfloat16*>(vn));
   return check_launch("attn prep_kernel");
@@ -368,7 +371,7 @@ extern "C" int jb_paged_attention(const uint16_t* q, const void* pool, int64_t p
     configured[dev] = true;
   }
   dim3 grid(b * attn::NKV, n / attn::BQ);
-  attn::paged_attention_kernel<<<grid, 256, SMEM, (cudaStream_t)stream>>>(
+  launch_pdl(attn::paged_attention_kernel, grid, 256, SMEM, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(q), static_cast<const uint8_t*>(pool), page_bytes, tables, table_stride,
       kv_entry, attn_layer, attn_layers, pos, reinterpret_cast<const __nv_bfloat16*>(kn),
       reinterpret_cast<const __nv_bfloat16*>(vn), reinterpret_cast<__nv_bfloat16*>(out), n,
@@ -387,7 +390,7 @@ extern "C" int jb_kv_scatter(const uint16_t* kn, const uint16_t* vn, int b, int 
                  (int64_t)attn_layers * 2 * attn::PAGE * attn::NKV * attn::HD * 2 <= page_bytes,
              "jb_kv_scatter: attention layer %d of %d", attn_layer, attn_layers);
   const size_t total = (size_t)b * n * 2 * (attn::NKV * attn::HD * 2 / 16);
-  attn::kv_scatter_kernel<<<(unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream>>>(
+  launch_pdl(attn::kv_scatter_kernel, (unsigned)((total + 255) / 256), 256, 0, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(kn), reinterpret_cast<const __nv_bfloat16*>(vn), b, n, real,
       static_cast<uint8_t*>(pool), page_bytes, out_tables, table_stride, kv_entry, attn_layer);
   return check_launch("kv_scatter_kernel");

@@ -86,6 +86,7 @@ __device__ __forceinline__ uint64_t mnmajor_desc(uint32_t saddr, uint32_t lbo) {
 __global__ void __launch_bounds__(THREADS, 1)
     attention_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_pool,
                      const __grid_constant__ CUtensorMap tm_kn, const __grid_constant__ CUtensorMap tm_vn, Params p) {
+  pdl_begin();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = smem_raw;
   if (smem_u32(smem) & 1023u) {   // uniform over the CTA: every thread returns before any barrier or allocation
@@ -416,6 +417,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 __global__ void __launch_bounds__(HD) combine_kernel(const float* __restrict__ part, int splits, int tokens,
                                                      const __nv_bfloat16* __restrict__ pr, int ldpr,
                                                      __nv_bfloat16* __restrict__ y, int ldy) {
+  pdl_begin();
   const int t = blockIdx.x / NQ, qh = blockIdx.x % NQ, d = threadIdx.x;
   const size_t rows = (size_t)tokens * NQ;
   const float* ml = part + (size_t)splits * rows * HD;
@@ -503,10 +505,10 @@ static int gated_impl(const uint16_t* q, const void* pool, int64_t pool_pages, i
                                            atc::ALLOC), "attention: shared memory attribute")))
     return st;
   dim3 grid(b * atc::NKV, n / atc::BQ, splits);
-  atc::attention_kernel<<<grid, atc::THREADS, atc::ALLOC, (cudaStream_t)stream>>>(tq, tpool, tkn, tvn, p);
+  launch_pdl(atc::attention_kernel, grid, atc::THREADS, atc::ALLOC, (cudaStream_t)stream, tq, tpool, tkn, tvn, p);
   if ((st = check_launch("attention_kernel (tcgen05)"))) return st;
   if (splits > 1) {
-    atc::combine_kernel<<<(unsigned)(t * atc::NQ), atc::HD, 0, (cudaStream_t)stream>>>(
+    launch_pdl(atc::combine_kernel, (unsigned)(t * atc::NQ), atc::HD, 0, (cudaStream_t)stream,
         part, splits, (int)t, reinterpret_cast<const __nv_bfloat16*>(pr), ldpr, reinterpret_cast<__nv_bfloat16*>(y),
         ldy);
     return check_launch("attention combine_kernel");

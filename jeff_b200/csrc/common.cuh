@@ -171,6 +171,35 @@ __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
 
+// ------------------------------------------------------------------ programmatic dependent launch
+//
+// Every kernel of the library starts with pdl_begin(): it waits until the grids it depends on have completed and
+// their memory is visible (a no-op for a launch without the attribute), then lets the stream's next launch start its
+// own launch and CTA dispatch while this grid runs. Nothing of a kernel touches global memory before that wait, so
+// launching with the attribute (launch_pdl) overlaps only launch latency, dispatch and the previous grid's tail with
+// the next grid's start; the order of every memory access is what a plain launch gives.
+__device__ __forceinline__ void pdl_begin() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+// whether launches carry the attribute (on unless the environment sets JB_NO_PDL)
+bool pdl_enabled();
+template <typename... Params, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
 // ------------------------------------------------------------------ device: one lane of a warp
 
 // true in exactly one active lane of the (converged) warp: the lane that issues a warp's single-thread operations

@@ -53,6 +53,7 @@ __global__ void __launch_bounds__(128) add_rms_kernel(const __nv_bfloat16* __res
                                                       const __nv_bfloat16* __restrict__ d,
                                                       const float* __restrict__ w1, __nv_bfloat16* xo,
                                                       __nv_bfloat16* __restrict__ h, int n) {
+  pdl_begin();
   __shared__ float scratch[32];
   const size_t row = blockIdx.x;
   const int nvec = n / 8;
@@ -96,6 +97,7 @@ __global__ void __launch_bounds__(128) add_rms_1024_kernel(const __nv_bfloat16* 
                                                            const __nv_bfloat16* __restrict__ d,
                                                            const float* __restrict__ w1, __nv_bfloat16* xo,
                                                            __nv_bfloat16* __restrict__ h, int rows) {
+  pdl_begin();
   constexpr int N = 1024;
   const int lane = threadIdx.x & 31;
   const size_t row = (size_t)blockIdx.x * 4 + (threadIdx.x >> 5);
@@ -142,6 +144,7 @@ __global__ void __launch_bounds__(128) rms_last_kernel(const __nv_bfloat16* __re
                                                        const int* __restrict__ last, int row_len, int n,
                                                        const float* __restrict__ w1,
                                                        __nv_bfloat16* __restrict__ hidden) {
+  pdl_begin();
   __shared__ float scratch[32];
   const size_t t = (size_t)blockIdx.x * row_len + last[blockIdx.x];
   const int nvec = n / 8;
@@ -176,6 +179,7 @@ __global__ void __launch_bounds__(128) rms_last_kernel(const __nv_bfloat16* __re
 
 __global__ void embed_kernel(const __nv_bfloat16* __restrict__ table, int vocab, int dim,
                              const int* __restrict__ ids, int t, __nv_bfloat16* __restrict__ x) {
+  pdl_begin();
   const int nvec = dim / 8;
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)t * nvec) return;
@@ -191,6 +195,7 @@ __device__ __forceinline__ float sigmoid(float g) { return 1.0f / (1.0f + expf(-
 
 __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int ldgu, int inter,
                                 __nv_bfloat16* __restrict__ y, int rows) {
+  pdl_begin();
   const int nvec = inter / 8;
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)rows * nvec) return;
@@ -207,6 +212,7 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gu, int ldgu, 
 // o (rows, 8, 256); gate of head h at pr[r, h * 512 + 256 + d]
 __global__ void gate_mul_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ pr, int ldpr,
                                 __nv_bfloat16* __restrict__ y, int rows) {
+  pdl_begin();
   constexpr int NVEC = 8 * 256 / 8;
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (size_t)rows * NVEC) return;
@@ -225,6 +231,7 @@ __global__ void gate_mul_kernel(const __nv_bfloat16* __restrict__ o, const __nv_
 __global__ void gated_norm_kernel(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ pr, int ldpr,
                                   int z_off, const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                                   int rows) {
+  pdl_begin();
   const size_t pair = ((size_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4;   // (token, head) index
   const int sub = threadIdx.x & 15;
   const bool live = pair < (size_t)rows * 16;
@@ -259,6 +266,7 @@ __global__ void __launch_bounds__(256) readout_kernel(const __nv_bfloat16* __res
                                                       const float* __restrict__ temp_pool,
                                                       const int* __restrict__ adapters, const int* __restrict__ counts,
                                                       float* __restrict__ probs) {
+  pdl_begin();
   __shared__ float logits[256];
   __shared__ float scratch[32];
   const int b = blockIdx.x;
@@ -306,12 +314,12 @@ extern "C" int jb_add_rms(const uint16_t* x, const uint16_t* d, const float* w1,
   JB_REQUIRE(!d || xo, "jb_add_rms: xo is needed with d");
   JB_REQUIRE(rows > 0 && n > 0 && n % 8 == 0 && n <= 128 * ew::RMS_MAX_VEC * 8, "jb_add_rms: rows %d, n %d", rows, n);
   if (n == 1024) {
-    ew::add_rms_1024_kernel<<<(rows + 3) / 4, 128, 0, (cudaStream_t)stream>>>(
+    launch_pdl(ew::add_rms_1024_kernel, (rows + 3) / 4, 128, 0, (cudaStream_t)stream,
         reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(d), w1,
         reinterpret_cast<__nv_bfloat16*>(xo), reinterpret_cast<__nv_bfloat16*>(h), rows);
     return check_launch("add_rms_1024_kernel");
   }
-  ew::add_rms_kernel<<<rows, 128, 0, (cudaStream_t)stream>>>(
+  launch_pdl(ew::add_rms_kernel, rows, 128, 0, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(d), w1,
       reinterpret_cast<__nv_bfloat16*>(xo), reinterpret_cast<__nv_bfloat16*>(h), n);
   return check_launch("add_rms_kernel");
@@ -322,7 +330,7 @@ extern "C" int jb_rms_last(const uint16_t* x, const uint16_t* d, const int32_t* 
   JB_REQUIRE(x && d && last && w1 && hidden, "jb_rms_last: null pointer");
   JB_REQUIRE(b > 0 && row_len > 0 && n > 0 && n % 8 == 0 && n <= 128 * ew::RMS_MAX_VEC * 8,
              "jb_rms_last: b %d, row_len %d, n %d", b, row_len, n);
-  ew::rms_last_kernel<<<b, 128, 0, (cudaStream_t)stream>>>(
+  launch_pdl(ew::rms_last_kernel, b, 128, 0, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(x), reinterpret_cast<const __nv_bfloat16*>(d), last, row_len, n, w1,
       reinterpret_cast<__nv_bfloat16*>(hidden));
   return check_launch("rms_last_kernel");
@@ -333,7 +341,7 @@ extern "C" int jb_embed(const uint16_t* table, int vocab, int dim, const int32_t
   JB_REQUIRE(table && ids && x, "jb_embed: null pointer");
   JB_REQUIRE(vocab > 0 && dim > 0 && dim % 8 == 0 && t > 0, "jb_embed: vocab %d, dim %d, t %d", vocab, dim, t);
   const size_t n = (size_t)t * (dim / 8);
-  ew::embed_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+  launch_pdl(ew::embed_kernel, blocks_for(n, 256), 256, 0, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(table), vocab, dim, ids, t, reinterpret_cast<__nv_bfloat16*>(x));
   return check_launch("embed_kernel");
 }
@@ -343,7 +351,7 @@ extern "C" int jb_silu_mul(const uint16_t* gu, int ldgu, int inter, uint16_t* y,
   JB_REQUIRE(rows > 0 && inter > 0 && inter % 8 == 0 && ldgu >= 2 * inter && ldgu % 8 == 0,
              "jb_silu_mul: rows %d, inter %d, ldgu %d", rows, inter, ldgu);
   const size_t n = (size_t)rows * (inter / 8);
-  ew::silu_mul_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+  launch_pdl(ew::silu_mul_kernel, blocks_for(n, 256), 256, 0, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(gu), ldgu, inter, reinterpret_cast<__nv_bfloat16*>(y), rows);
   return check_launch("silu_mul_kernel");
 }
@@ -352,7 +360,7 @@ extern "C" int jb_gate_mul(const uint16_t* o, const uint16_t* pr, int ldpr, uint
   JB_REQUIRE(o && pr && y, "jb_gate_mul: null pointer");
   JB_REQUIRE(rows > 0 && ldpr >= 4096 && ldpr % 8 == 0, "jb_gate_mul: rows %d, ldpr %d", rows, ldpr);
   const size_t n = (size_t)rows * 256;
-  ew::gate_mul_kernel<<<blocks_for(n, 256), 256, 0, (cudaStream_t)stream>>>(
+  launch_pdl(ew::gate_mul_kernel, blocks_for(n, 256), 256, 0, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(pr), ldpr,
       reinterpret_cast<__nv_bfloat16*>(y), rows);
   return check_launch("gate_mul_kernel");
@@ -367,7 +375,7 @@ extern "C" int jb_gated_norm(const uint16_t* o, const uint16_t* pr, int ldpr, in
                reinterpret_cast<uintptr_t>(y)) & 15) == 0,
              "jb_gated_norm: o, pr, w and y must be 16-byte aligned");
   const size_t threads = (size_t)rows * 16 * 16;   // 16 per (token, head)
-  ew::gated_norm_kernel<<<blocks_for(threads, 256), 256, 0, (cudaStream_t)stream>>>(
+  launch_pdl(ew::gated_norm_kernel, blocks_for(threads, 256), 256, 0, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(o), reinterpret_cast<const __nv_bfloat16*>(pr), ldpr, z_off,
       reinterpret_cast<const __nv_bfloat16*>(w), reinterpret_cast<__nv_bfloat16*>(y), rows);
   return check_launch("gated_norm_kernel");
@@ -378,7 +386,7 @@ extern "C" int jb_readout_rows(const uint16_t* hidden, const uint16_t* readout_p
                                float* probs, void* stream) {
   JB_REQUIRE(hidden && readout_pool && temp_pool && adapters && counts && probs, "jb_readout_rows: null pointer");
   JB_REQUIRE(b > 0 && pool_rows > 0, "jb_readout_rows: b %d, pool_rows %d", b, pool_rows);
-  ew::readout_kernel<<<b, 256, 0, (cudaStream_t)stream>>>(
+  launch_pdl(ew::readout_kernel, b, 256, 0, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(hidden), reinterpret_cast<const __nv_bfloat16*>(readout_pool),
       pool_rows, temp_pool, adapters, counts, probs);
   return check_launch("readout_kernel");

@@ -41,6 +41,7 @@ __global__ void __launch_bounds__(128) prep_kernel(const __nv_bfloat16* __restri
                                                    __nv_bfloat16* __restrict__ v, float* __restrict__ g,
                                                    __nv_bfloat16* __restrict__ beta, const int* __restrict__ real,
                                                    const int* __restrict__ out_tables, int out_table_stride) {
+  pdl_begin();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = blockIdx.z, slice = blockIdx.y;
   const int t0 = (blockIdx.x * 4 + warp) * PT;
@@ -154,6 +155,7 @@ __global__ void __launch_bounds__(256) scan_kernel(const __nv_bfloat16* __restri
                                                    int table_stride, int first_head, int heads_per_page,
                                                    const int* __restrict__ last, const int* __restrict__ out_tables,
                                                    int out_table_stride) {
+  pdl_begin();
   constexpr int HALF = HDIM / 2;
   __shared__ __align__(16) float kq[2][2][HDIM];
   const int row = blockIdx.x / NH, h = blockIdx.x % NH;
@@ -243,7 +245,7 @@ extern "C" int jb_gdn_prep_rows(const uint16_t* pr, int ldpr, int t, int n, void
   JB_REQUIRE(!out_tables || real, "jb_gdn_prep_rows: out_tables needs real");
   const int chunks = (n + gdn::PT - 1) / gdn::PT;
   dim3 grid((chunks + 3) / 4, 3 * gdn::NH + 1, t / n);
-  gdn::prep_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(
+  launch_pdl(gdn::prep_kernel, grid, 128, 0, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(pr), ldpr, n, static_cast<uint8_t*>(pool), page_bytes, tables,
       table_stride, conv_entry, conv_slot, conv_w, a_neg, dt_bias, reinterpret_cast<__nv_bfloat16*>(q),
       reinterpret_cast<__nv_bfloat16*>(k), reinterpret_cast<__nv_bfloat16*>(v), g,
@@ -262,7 +264,7 @@ extern "C" int jb_gdn_scan_recurrent(const uint16_t* q, const uint16_t* k, const
              (long long)page_bytes);
   JB_REQUIRE(first_head >= 0 && (first_head + gdn::NH - 1) / heads_per_page < table_stride,
              "jb_gdn_scan_recurrent: heads %d.. reach past the block table (%d entries)", first_head, table_stride);
-  gdn::scan_kernel<<<b * gdn::NH, 256, 0, (cudaStream_t)stream>>>(
+  launch_pdl(gdn::scan_kernel, b * gdn::NH, 256, 0, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
       reinterpret_cast<const __nv_bfloat16*>(v), g, reinterpret_cast<const __nv_bfloat16*>(beta),
       reinterpret_cast<__nv_bfloat16*>(o), n, static_cast<uint8_t*>(pool), page_bytes, tables, table_stride,

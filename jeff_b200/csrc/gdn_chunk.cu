@@ -403,6 +403,7 @@ __global__ void __launch_bounds__(256, 1) chunk_kernel(const __nv_bfloat16* __re
                                                        int table_stride, int first_head, int heads_per_page,
                                                        const int* __restrict__ last,
                                                        const int* __restrict__ out_tables, int out_table_stride) {
+  pdl_begin();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>(smem_raw);
   const int row = blockIdx.x / NH, h = blockIdx.x % NH;
@@ -508,6 +509,7 @@ __global__ void __launch_bounds__(256, 1) layer_kernel(const __nv_bfloat16* __re
                                                        __nv_bfloat16* __restrict__ y, int ldy,
                                                        const int* __restrict__ last, const int* __restrict__ real,
                                                        const int* __restrict__ out_tables, int out_table_stride) {
+  pdl_begin();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   LayerSmem& L = *reinterpret_cast<LayerSmem*>(smem_raw);
   Smem& sm = L.scan;
@@ -736,7 +738,7 @@ extern "C" int jb_gdn_scan(const uint16_t* q, const uint16_t* k, const uint16_t*
   constexpr int SMEM = (int)sizeof(gdnc::Smem);
   int st = gdnc::configure(gdnc::chunk_kernel, SMEM, "gdn chunk_kernel");
   if (st) return st;
-  gdnc::chunk_kernel<<<b * gdnc::NH, 256, SMEM, (cudaStream_t)stream>>>(
+  launch_pdl(gdnc::chunk_kernel, b * gdnc::NH, 256, SMEM, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(q), reinterpret_cast<const __nv_bfloat16*>(k),
       reinterpret_cast<const __nv_bfloat16*>(v), g, reinterpret_cast<const __nv_bfloat16*>(beta),
       reinterpret_cast<__nv_bfloat16*>(o), n, static_cast<uint8_t*>(pool), page_bytes, tables, table_stride,
@@ -768,7 +770,7 @@ extern "C" int jb_gdn_layer(const uint16_t* pr, int ldpr, int t, int n, void* po
   static_assert(SMEM <= 227 * 1024, "shared memory");
   int st = gdnc::configure(gdnc::layer_kernel, SMEM, "gdn layer_kernel");
   if (st) return st;
-  gdnc::layer_kernel<<<(t / n) * gdnc::NH, 256, SMEM, (cudaStream_t)stream>>>(
+  launch_pdl(gdnc::layer_kernel, (t / n) * gdnc::NH, 256, SMEM, (cudaStream_t)stream,
       reinterpret_cast<const __nv_bfloat16*>(pr), ldpr, n, static_cast<uint8_t*>(pool), page_bytes, tables,
       table_stride, first_head, heads_per_page, conv_entry, conv_slot, conv_w, a_neg, dt_bias,
       reinterpret_cast<const __nv_bfloat16*>(gnorm_w), reinterpret_cast<__nv_bfloat16*>(y), ldy, last, real,

@@ -102,6 +102,7 @@ __global__ void __launch_bounds__(THREADS, 2)
                 uint8_t* __restrict__ pool, int64_t page_bytes, const int* __restrict__ tables, int table_stride,
                 int first_head, int heads_per_page, const int* __restrict__ last, const int* __restrict__ out_tables,
                 int out_table_stride, int* err) {
+  pdl_begin();
   extern __shared__ uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* kq = sm + OFF_KQ;
@@ -643,7 +644,7 @@ extern "C" int jb_gdn_scan_tc(const uint16_t* q, const uint16_t* k, const uint16
   if (st) return st;
   st = gdnc::configure(gdnt::scan_kernel, gdnt::ALLOC, "gdn scan_kernel (tcgen05)");
   if (st) return st;
-  gdnt::scan_kernel<<<b * gdnc::NH, gdnt::THREADS, gdnt::ALLOC, (cudaStream_t)stream>>>(
+  launch_pdl(gdnt::scan_kernel, b * gdnc::NH, gdnt::THREADS, gdnt::ALLOC, (cudaStream_t)stream,
       tq, tk, tv, to, g, reinterpret_cast<const __nv_bfloat16*>(beta), n, static_cast<uint8_t*>(pool), page_bytes,
       tables, table_stride, first_head, heads_per_page, last, out_tables, out_table_stride, device_status_word());
   return check_launch("gdn scan_kernel (tcgen05)");

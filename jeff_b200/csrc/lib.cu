@@ -56,6 +56,11 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
+bool pdl_enabled() {
+  static const bool on = getenv("JB_NO_PDL") == nullptr;
+  return on;
+}
+
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, uint64_t inner, uint64_t outer,
                  uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swizzle) {
   auto fn = encode_fn();

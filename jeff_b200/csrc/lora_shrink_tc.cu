@@ -52,6 +52,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     shrink_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_a, int M, int K,
                   int R, int pool_rows, const int* __restrict__ adapters, int row_len, __nv_bfloat16* __restrict__ mid,
                   int* err) {
+  pdl_begin();
   using L = Layout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -220,6 +221,7 @@ __global__ void __launch_bounds__(DOT_THREADS) dot_kernel(const __nv_bfloat16* _
                                                           int pool_rows, const int* __restrict__ adapters,
                                                           int row_len, const __nv_bfloat16* __restrict__ A,
                                                           __nv_bfloat16* __restrict__ mid) {
+  pdl_begin();
   const int t = blockIdx.x;
   const int r = blockIdx.y * DOT_ROWS + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (r >= R) return;   // whole warps
@@ -249,7 +251,7 @@ __global__ void __launch_bounds__(DOT_THREADS) dot_kernel(const __nv_bfloat16* _
 int launch(const __nv_bfloat16* x, int m, int k, const __nv_bfloat16* a, int rank, int pool_rows,
            const int* adapters, int row_len, __nv_bfloat16* mid, cudaStream_t stream) {
   if (m <= DOT_MAX_M) {
-    dot_kernel<<<dim3(m, (rank + DOT_ROWS - 1) / DOT_ROWS), DOT_THREADS, 0, stream>>>(x, k, rank, pool_rows,
+    launch_pdl(dot_kernel, dim3(m, (rank + DOT_ROWS - 1) / DOT_ROWS), DOT_THREADS, 0, stream, x, k, rank, pool_rows,
                                                                                      adapters, row_len, a, mid);
     return check_launch("lora shrink dot_kernel");
   }
@@ -264,7 +266,7 @@ int launch(const __nv_bfloat16* x, int m, int k, const __nv_bfloat16* a, int ran
   if (st) return st;
   cudaError_t e = cudaFuncSetAttribute(shrink_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, Layout::ALLOC);
   if (e != cudaSuccess) return status_of(e, "lora shrink_kernel (tcgen05): shared memory attribute");
-  shrink_kernel<<<(m + TM - 1) / TM, THREADS, Layout::ALLOC, stream>>>(tx, ta, m, k, rank, pool_rows, adapters,
+  launch_pdl(shrink_kernel, (m + TM - 1) / TM, THREADS, Layout::ALLOC, stream, tx, ta, m, k, rank, pool_rows, adapters,
                                                                        row_len, mid, device_status_word());
   return check_launch("lora shrink_kernel (tcgen05)");
 }

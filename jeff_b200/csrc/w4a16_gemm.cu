@@ -180,6 +180,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                       const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
                       const __grid_constant__ CUtensorMap tm_mid, const __grid_constant__ CUtensorMap tm_lb,
                       Params p) {
+  pdl_begin();
   using L = Layout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -615,6 +616,7 @@ __global__ void __launch_bounds__(128) lora_shrink_kernel(const __nv_bfloat16* _
                                                           const __nv_bfloat16* __restrict__ A, int pool_rows,
                                                           const int* __restrict__ adapters, int row_len,
                                                           __nv_bfloat16* __restrict__ mid) {
+  pdl_begin();
   constexpr int R = NB * 8;
   __shared__ float part[4][16][R + 1];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -705,6 +707,7 @@ __global__ void __launch_bounds__(SH_THREADS) lora_shrink_staged_kernel(const __
                                                                  const __nv_bfloat16* __restrict__ A, int pool_rows,
                                                                  const int* __restrict__ adapters, int row_len,
                                                                  __nv_bfloat16* __restrict__ mid) {
+  pdl_begin();
   constexpr int R = NB * 8;
   extern __shared__ __align__(16) uint8_t sh_smem[];
   __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(sh_smem);   // [SH_STAGES][SH_ROWS][SH_PITCH]
@@ -822,7 +825,7 @@ int launch_shrink_staged(const __nv_bfloat16* x, int m, int k, const __nv_bfloat
   cudaError_t e = cudaFuncSetAttribute(lora_shrink_staged_kernel<NB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        bytes);
   if (e != cudaSuccess) return status_of(e, "lora_shrink_staged_kernel: shared memory attribute");
-  lora_shrink_staged_kernel<NB><<<(m + SH_ROWS - 1) / SH_ROWS, SH_THREADS, bytes, st>>>(x, m, k, a, pool_rows, adapters,
+  launch_pdl(lora_shrink_staged_kernel<NB>, (m + SH_ROWS - 1) / SH_ROWS, SH_THREADS, bytes, st, x, m, k, a, pool_rows, adapters,
                                                                                  row_len, mid);
   return check_launch("lora_shrink_staged_kernel");
 }
@@ -832,6 +835,7 @@ int launch_shrink_staged(const __nv_bfloat16* x, int m, int k, const __nv_bfloat
 __global__ void int4_dequant_kernel(const int32_t* __restrict__ words, const __nv_bfloat16* __restrict__ scales,
                                     const __nv_bfloat16* __restrict__ zeros, int K, int columns, int group,
                                     __nv_bfloat16* __restrict__ out) {
+  pdl_begin();
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int i = blockIdx.y;   // word row: inputs 8i .. 8i + 7
   if (c >= columns) return;
@@ -858,12 +862,13 @@ int launch(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ts, 
   if (e != cudaSuccess) return status_of(e, "w4a16: SM count");
   const int items = p.m_tiles * p.n_tiles * p.k_split;
   const int grid = items < sms ? items : sms;
-  kernel<<<grid, THREADS, Layout::ALLOC, stream>>>(tx, tw, ts, tz, tm, tl, p);
+  launch_pdl(kernel, grid, THREADS, Layout::ALLOC, stream, tx, tw, ts, tz, tm, tl, p);
   return check_launch("w4a16_lora_kernel");
 }
 
 // reference word layout (input 8i + j in bits 4j) -> kernel layout (input j in slot kernel_slot(j)); in place ok
 __global__ void int4_repack_kernel(const int32_t* __restrict__ in, int32_t* __restrict__ out, size_t n) {
+  pdl_begin();
   const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const uint32_t w = static_cast<uint32_t>(in[i]);
@@ -889,7 +894,7 @@ extern "C" int jb_int4_dequant(const int32_t* words, const uint16_t* scales, con
   JB_REQUIRE(group == 64 || group == 128, "jb_int4_dequant: group %d (64 or 128)", group);
   JB_REQUIRE(k % group == 0, "jb_int4_dequant: k %d is not a multiple of the group %d", k, group);
   dim3 grid((columns + 127) / 128, k / 8);
-  w4::int4_dequant_kernel<<<grid, 128, 0, (cudaStream_t)stream>>>(
+  launch_pdl(w4::int4_dequant_kernel, grid, 128, 0, (cudaStream_t)stream,
       words, reinterpret_cast<const __nv_bfloat16*>(scales), reinterpret_cast<const __nv_bfloat16*>(zeros), k,
       columns, group, reinterpret_cast<__nv_bfloat16*>(out));
   return check_launch("int4_dequant_kernel");
@@ -929,10 +934,10 @@ extern "C" int jb_lora_shrink(const uint16_t* x, int m, int k, const uint16_t* l
              row_len);
   dim3 grid(m / 16);
   switch (rank) {
-    case 16: w4::lora_shrink_kernel<2><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
-    case 32: w4::lora_shrink_kernel<4><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
-    case 48: w4::lora_shrink_kernel<6><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
-    case 64: w4::lora_shrink_kernel<8><<<grid, 128, 0, st>>>(xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
+    case 16: launch_pdl(w4::lora_shrink_kernel<2>, grid, 128, 0, st, xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
+    case 32: launch_pdl(w4::lora_shrink_kernel<4>, grid, 128, 0, st, xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
+    case 48: launch_pdl(w4::lora_shrink_kernel<6>, grid, 128, 0, st, xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
+    case 64: launch_pdl(w4::lora_shrink_kernel<8>, grid, 128, 0, st, xb, m, k, ab, pool_rows, adapters, row_len, mb); break;
     default: set_error("jb_lora_shrink: rank %d (16, 32, 48 or 64)", rank); return JB_EINVAL;
   }
   return check_launch("lora_shrink_kernel");
@@ -1091,7 +1096,7 @@ extern "C" int jb_int4_repack(const int32_t* words, int32_t* out, int k, int col
   JB_REQUIRE(words && out, "jb_int4_repack: null pointer");
   JB_REQUIRE(k > 0 && k % 8 == 0 && columns > 0, "jb_int4_repack: k %d, columns %d", k, columns);
   const size_t n = (size_t)(k / 8) * columns;
-  w4::int4_repack_kernel<<<(unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream>>>(words, out, n);
+  launch_pdl(w4::int4_repack_kernel, (unsigned)((n + 255) / 256), 256, 0, (cudaStream_t)stream, words, out, n);
   return check_launch("int4_repack_kernel");
 }
 

@@ -108,6 +108,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     w4a16_tmem_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                       const __grid_constant__ CUtensorMap tm_s, const __grid_constant__ CUtensorMap tm_z,
                       const __grid_constant__ CUtensorMap tm_mid, Params p) {
+  pdl_begin();
   using L = Layout;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -415,12 +416,12 @@ inline int launch(const uint16_t* x, int m, int k, const int32_t* words, const u
     if ((st = status_of(cudaFuncSetAttribute(w4a16_tmem_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Layout::ALLOC), "w4a16 tmem: shared memory attribute")))
       return st;
-    w4a16_tmem_kernel<true><<<grid, THREADS, Layout::ALLOC, stream>>>(tx, tw, ts, tz, tm, p);
+    launch_pdl(w4a16_tmem_kernel<true>, grid, THREADS, Layout::ALLOC, stream, tx, tw, ts, tz, tm, p);
   } else {
     if ((st = status_of(cudaFuncSetAttribute(w4a16_tmem_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              Layout::ALLOC), "w4a16 tmem: shared memory attribute")))
       return st;
-    w4a16_tmem_kernel<false><<<grid, THREADS, Layout::ALLOC, stream>>>(tx, tw, ts, tz, tm, p);
+    launch_pdl(w4a16_tmem_kernel<false>, grid, THREADS, Layout::ALLOC, stream, tx, tw, ts, tz, tm, p);
   }
   return check_launch("w4a16_tmem_kernel");
 }
