@@ -52,6 +52,26 @@ def test_bad_arguments_are_refused_before_any_launch(lib: ctypes.CDLL) -> None:
         _lib.call("jb_lora_shrink", p, 32, 64, p, 20, 1, p, 32, p, None)
 
 
+def test_small_pass_product_refusals(lib: ctypes.CDLL) -> None:
+    """jb_w4a16_lora_small refuses, before any launch, what its one-wave cluster form cannot hold: more than two LoRA
+    rows, a slice count that is not 1, 2, 4 or 8 or leaves a slice's CTA a ragged token count, and a slice whose K
+    blocks do not fit in shared memory."""
+    p = ctypes.c_void_p(16)
+    small = lib.jb_w4a16_lora_small
+    # 48 tokens in rows of 16: three LoRA rows
+    assert small(p, 48, 3584, p, p, None, 128, 1024, 1024, p, p, 16, 2, p, 16, p, 1024, 0, 0, None) == -1
+    assert b"LoRA rows" in lib.jb_last_error()
+    # 48 tokens over 8 slices: 6 tokens per slice's CTA
+    assert small(p, 48, 3584, p, p, None, 128, 1024, 1024, None, None, 0, 0, None, 48, p, 1024, 0, 8, None) == -1
+    assert b"multiple of 4" in lib.jb_last_error()
+    assert small(p, 48, 3584, p, p, None, 128, 1024, 1024, None, None, 0, 0, None, 48, p, 1024, 0, 3, None) == -1
+    assert b"1, 2, 4 or 8" in lib.jb_last_error()
+    # one slice of all 56 K blocks
+    assert small(p, 48, 3584, p, p, None, 128, 1024, 1024, None, None, 0, 0, None, 48, p, 1024, 0, 1, None) == -1
+    assert b"shared memory" in lib.jb_last_error()
+
+
 def test_the_product_library_has_no_stage_trace(lib: ctypes.CDLL) -> None:
-    """The stage-trace read-out exists only in measurement builds (-DJB_TRACE), not in the product library."""
-    assert not hasattr(lib, "jb_stage_trace_read")
+    """The trace read-outs exist only in measurement builds (-DJB_TRACE), not in the product library."""
+    for name in ("jb_stage_trace_read", "jb_prod_trace_read", "jb_small_trace_read", "jb_small_span_read"):
+        assert not hasattr(lib, name), name
